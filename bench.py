@@ -1,0 +1,515 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 small-batch projection path (one JSON line on rank 0).
+
+Headline workload: the 32-layer Llama-3-8B-shaped
+projection chain at M=1 in one CUDA graph per token, column-sharded over the
+GPUs with an all-gather of `up` and `down` outputs per layer. value = tokens/s
+of the whole job (strong scaling: the per-token work is fixed as N grows).
+Weights are 13.96 GB per token step, far larger than the 126 MB L2, so every
+step reads HBM without an explicit flush.
+
+Also reported (N=1): µs / achieved GB/s for configs 1-4 next to cuBLAS on the
+same shapes (`projections`), the roofline of the dominant kernel, the
+end-to-end rate through the public API with host buffers (`e2e`), the CPU
+oracle timed on the host (`cpu_baseline`), and SM clocks sampled during the
+timed region.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+"""
+
+from __future__ import annotations
+
+import argparse
+import hashlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+METRIC = "achieved HBM GB/s vs 8 TB/s & µs/projection at M=1..16; chain tok/s 1/2/4/8 GPU"
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_HBM_GBS = 6650.0
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    try:
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during a timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id):
+        self.gpu_id = gpu_id
+        self.samples = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "50", "-i", str(self.gpu_id)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return self
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.perf_counter(), [p.strip() for p in line.split(",")]))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+
+    def summary(self, t0, t1):
+        rows = [s for (t, s) in self.samples if t0 - 0.06 <= t <= t1 + 0.06 and len(s) >= 9]
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][2]),
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((num(r[3]) or 0.0) for r in rows)}
+
+
+# ---------------------------------------------------------------- helpers
+
+def gpu_uuid(torch, device):
+    try:
+        return "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+    except Exception:
+        return str(device)
+
+
+def all_max(torch, value, world):
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def graph_of(torch, fn, stream):
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        fn()
+    torch.cuda.current_stream().wait_stream(stream)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        fn()
+    return graph
+
+
+def time_graph(torch, graph, calls, rounds):
+    """Median µs per call over `rounds` replays of a graph of `calls` calls."""
+    times = []
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    for _ in range(rounds):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        graph.replay()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b) * 1000.0 / calls)
+    return statistics.median(times)
+
+
+# ---------------------------------------------------------------- per-config projections (N=1)
+
+def ring_count(nbytes):
+    return max(8, math.ceil(max(2 << 30, 16 * L2_BYTES) / nbytes))
+
+
+def bench_projections(torch, peak, quick=False):
+    """Configs 1-4 through the public API over cold-L2 weight rings, with cuBLAS
+    (torch F.linear) on the same shapes (dequantized BF16 weights for INT8/FP4)."""
+    import torch.nn.functional as F
+
+    from klab_b200 import compressed_bf16 as cb
+    from klab_b200 import fp4, int8_weights
+
+    dev = torch.device("cuda")
+    stream = torch.cuda.Stream()
+    gen = torch.Generator(device=dev)
+    results = []
+    rounds = 5 if quick else 15
+
+    def record(name, m, n, k, nbytes, fn_ours, fn_vendor, ring):
+        g = graph_of(torch, lambda: [fn_ours(i) for i in range(ring)], stream)
+        us = time_graph(torch, g, ring, rounds)
+        del g
+        row = {"config": name, "m": m, "n": n, "k": k, "bytes": nbytes, "us": round(us, 3),
+               "gbs": round(nbytes / us / 1e3, 1), "frac_of_measured_peak": round(nbytes / us / 1e3 / peak, 4)}
+        if fn_vendor is not None:
+            gv = graph_of(torch, lambda: [fn_vendor(i) for i in range(ring)], stream)
+            vus = time_graph(torch, gv, ring, rounds)
+            del gv
+            row["cublas_us"] = round(vus, 3)
+            row["speedup_vs_cublas"] = round(vus / us, 3)
+        results.append(row)
+        torch.cuda.empty_cache()
+
+    def bf16_normal(shape, std, seed):
+        gen.manual_seed(seed)
+        return torch.randn(shape, generator=gen, device=dev).mul_(std).to(torch.bfloat16)
+
+    # C1: BF16 4096 x 4096, M = 1
+    n = k = 4096
+    w = bf16_normal((n, k), 0.02, 1)
+    nbytes = n * k * 2 + k * 2 + n * 2
+    ring = ring_count(n * k * 2)
+    ws = [w.clone() for _ in range(ring)]
+    x = bf16_normal((1, k), 0.02, 2)
+    outs = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+    record("c1_bf16_m1", 1, n, k, nbytes,
+           lambda i: cb.raw_linear(x, ws[i], threads=128, vector=8, output_dtype="bf16", out=outs),
+           lambda i: F.linear(x, ws[i]), ring)
+    del ws, w
+
+    # C2: INT8 per-row, K=4096, N=14336, M in {1, 4, 16}
+    n, k = 14336, 4096
+    gen.manual_seed(3)
+    w32 = torch.randn((n, k), generator=gen, device=dev).mul_(0.02)
+    q = int8_weights.quantize_weights_per_row(w32)
+    deq = q.dequantize().to(torch.bfloat16)
+    del w32
+    ring = ring_count(n * k)
+    codes = [q.codes.clone() for _ in range(ring)]
+    vring = max(4, math.ceil(ring / 2))
+    deqs = [deq.clone() for _ in range(vring)]
+    for m in ((1,) if quick else (1, 4, 16)):
+        x = bf16_normal((m, k), 1.0, 4 + m)
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        nbytes = n * k + n * 4 + m * k * 2 + m * n * 2
+        record(f"c2_int8_row_m{m}", m, n, k, nbytes,
+               lambda i: int8_weights.fused_linear(x, codes[i], q.scales, out=out, output_dtype=torch.bfloat16),
+               lambda i: F.linear(x, deqs[i % vring]), ring)
+    del codes, deqs, deq, q
+
+    # C3: FP4 E2M1 with FP16 scales per 32, K=N=8192, M in {1, 8}
+    n = k = 8192
+    gen.manual_seed(5)
+    w32 = torch.randn((n, k), generator=gen, device=dev).mul_(0.02)
+    q = fp4.quantize_weights_f16(w32)
+    deq = q.dequantize().to(torch.bfloat16)
+    del w32
+    ring = ring_count(n * k // 2 + n * k // 16)
+    packs = [(q.packed.clone(), q.scales.clone()) for _ in range(ring)]
+    vring = max(4, math.ceil(ring / 4))
+    deqs = [deq.clone() for _ in range(vring)]
+    for m in ((1,) if quick else (1, 8)):
+        x = bf16_normal((m, k), 1.0, 6 + m)
+        out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+        nbytes = n * k // 2 + n * k // 16 + m * k * 2 + m * n * 2
+        record(f"c3_fp4_f16s32_m{m}", m, n, k, nbytes,
+               lambda i: fp4.fused_linear(x, packs[i][0], packs[i][1], None, out=out, output_dtype=torch.bfloat16),
+               lambda i: F.linear(x, deqs[i % vring]), ring)
+    del packs, deqs, deq, q
+
+    # C4: lossless-coded BF16, 8 independent 4096 x 4096 layers
+    n = k = 4096
+    layers = []
+    for seed in range(8):
+        w = bf16_normal((n, k), 0.02, 100 + seed)
+        bits = w.view(torch.int16).cpu().numpy().view("uint16")
+        layers.append((cb.upload(cb.pack_bits(bits), dev), w))
+    per = layers[0][0].storage_bytes
+    ring = ring_count(per)
+    coded = [layers[i % 8][0] for i in range(8)]
+    coded += [cb.PackedBF16(coded[i % 8].payload.clone(), coded[i % 8].metadata.clone(), n, k,
+                            coded[i % 8].source_sha256, 1, coded[i % 8].module) for i in range(8, ring)]
+    raws = [layers[i % 8][1] for i in range(8)] + [layers[i % 8][1].clone() for i in range(8, ring_count(n * k * 2))]
+    x = bf16_normal((1, k), 1.0, 9)
+    out = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+    storage = sum(c.storage_bytes for c in coded) / len(coded)
+    nbytes = int(storage) + k * 2 + n * 2
+    record("c4_lossless_bf16_m1", 1, n, k, nbytes,
+           lambda i: cb.fused_linear(x, coded[i], threads=128, vector=8, output_dtype="bf16", out=out),
+           lambda i: F.linear(x, raws[i % len(raws)]), ring)
+    results[-1]["storage_fraction"] = round(storage / (n * k * 2), 4)
+    results[-1]["effective_bf16_gbs"] = round((n * k * 2 + k * 2 + n * 2) / results[-1]["us"] / 1e3, 1)
+    del coded, raws, layers
+    torch.cuda.empty_cache()
+    return results
+
+
+# ---------------------------------------------------------------- dominant kernel roofline
+
+def bench_dominant_kernel(torch, chain, peak, rounds=10):
+    """Average duration of the chain's gate projection (the largest BF16 GEMV),
+    timed with CUDA events on its launch stream over the chain's 32 distinct gate
+    weights (cold L2), inside a CUDA graph."""
+    from klab_b200 import _native
+
+    shape = chain.shape
+    gates = [layer["gate"] for layer in chain.layers]
+    h = chain.hbuf[0]
+    out = chain.a_out["gate"]
+    n_shard = gates[0][1][1] - gates[0][1][0]
+    stream = torch.cuda.Stream()
+
+    def run():
+        for w, rows, n in gates:
+            _native.gemv(_native.W_BF16, _native.DT_BF16, h, w, None, None, out[:, rows[0]:], _native.DT_BF16,
+                         h.shape[0], n_shard, shape.hidden, ldo=n)
+
+    g = graph_of(torch, run, stream)
+    us = time_graph(torch, g, len(gates), rounds)
+    del g
+    nbytes = n_shard * shape.hidden * 2 + shape.hidden * 2 + n_shard * 2
+    achieved = nbytes / us / 1e3
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "traffic": None, "kernel": "stream_gemv_kernel<W_BF16,X_BF16,SMEM,1>",
+            "launch": f"gate {n_shard}x{shape.hidden} bf16, M=1", "bytes_per_launch": nbytes,
+            "us_per_launch": round(us, 3)}
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+
+def cpu_oracle_tok_s(seconds=10.0):
+    """The CPU oracle's FP64 projection (oracle.gemv.projection64 + round_bf16_bits)
+    timed on one decoder layer of the chain (7 projections), scaled to tokens/s
+    for 32 layers. Weights are pre-widened to FP64 outside the timed region."""
+    import numpy as np
+
+    from oracle import bf16 as ob
+    from oracle import gemv as og
+
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max([p.get("num_threads", 1) for p in threadpool_info()] or [os.cpu_count() or 1])
+    except Exception:
+        cores = os.cpu_count() or 1
+    shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
+    rng = np.random.default_rng(0)
+    weights = [ob.bf16_values(og.normal_bf16_bits(i, shape, 0.02)) for i, shape in enumerate(shapes)]
+    x = ob.bf16_values(og.normal_bf16_bits(99, (1, 4096), 1.0))
+    up = ob.bf16_values(og.normal_bf16_bits(98, (1, 14336), 1.0))
+    layers = 0
+    t0 = time.perf_counter()
+    while True:
+        for i, w in enumerate(weights):
+            src = up if i == 6 else x
+            ob.round_bf16_bits(og.projection64(src, w))
+        layers += 1
+        if time.perf_counter() - t0 >= seconds:
+            break
+    elapsed = time.perf_counter() - t0
+    del rng
+    per_token = elapsed / layers * 32
+    return {"value": round(1.0 / per_token, 4), "unit": "tok/s", "cores": int(cores), "kind": "port",
+            "sample": f"{layers} passes over one 7-projection decoder layer (FP64 oracle, 218M weights), "
+                      f"{elapsed:.1f} s, scaled x32 layers per token"}
+
+
+# ---------------------------------------------------------------- reference arm
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    seconds = max(3.0, min(30.0, 2.0 * (args.steps + args.warmup) / 10.0))
+    base = cpu_oracle_tok_s(seconds)
+    line = {"metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(1000.0 / base["value"], 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "c5_chain_llama3_8b_shapes_32_layers_m1", "layers": 32, "M": 1,
+                       "hidden": 4096, "ffn": 14336, "kv": 1024},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- main
+
+def main(argv=None):
+    parser = argparse.ArgumentParser(description="B200 projection-path benchmark")
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=300)
+    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    parser.add_argument("--layers", type=int, default=32)
+    parser.add_argument("--no-projections", action="store_true", help="skip the per-config projection lines")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--quick", action="store_true", help="fewer rounds and shapes (smoke runs)")
+    parser.add_argument("--gather", choices=("nccl",), default="nccl")
+    args = parser.parse_args(argv)
+    if args.warmup < 3:
+        parser.error("--warmup must be >= 3")
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+
+    torch.cuda.set_device(local)
+    group = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+        group = dist.group.WORLD
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_bf16_reduced_precision_reduction = False
+
+    from klab_b200 import _native
+    from klab_b200.chain import ChainShape, ProjectionChain
+
+    peak, peak_kind = measured_peak()
+    shape = ChainShape(layers=args.layers)
+    chain = ProjectionChain(shape, rank=rank, world=world, group=group, seed=0)
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(1234)
+    x = torch.randn((1, shape.hidden), generator=gen, device="cuda").to(torch.bfloat16)
+    out = chain.capture(x)
+    for _ in range(args.warmup):
+        chain.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    sampler = ClockSampler(gpu_uuid(torch, local)).start() if rank == 0 else None
+    time.sleep(0.2 if sampler else 0.0)
+    barrier(world)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for _ in range(args.steps):
+        chain.replay()
+    e1.record(stream)
+    e1.synchronize()
+    t1 = time.perf_counter()
+    barrier(world)
+    torch.cuda.synchronize()
+    local_s = e0.elapsed_time(e1) / 1000.0
+    step_s = all_max(torch, local_s, world)
+    clocks = None
+    if sampler is not None:
+        time.sleep(0.1)
+        sampler.stop()
+        clocks = sampler.summary(t0, t1)
+    digest = hashlib.sha256(out.view(torch.int16).cpu().numpy().tobytes()).hexdigest()
+
+    # End to end through the public API: pinned host token in, host result out, per step.
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    e2e_steps = max(20, args.steps // 3)
+    barrier(world)
+    torch.cuda.synchronize()
+    t2 = time.perf_counter()
+    for _ in range(e2e_steps):
+        chain.static_x.copy_(x_host, non_blocking=True)
+        chain.replay()
+        y_host.copy_(out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    t3 = time.perf_counter()
+    e2e_s = all_max(torch, t3 - t2, world)
+
+    roofline = bench_dominant_kernel(torch, chain, peak)
+    roofline["peak_kind"] = peak_kind
+    status = _native.device_status(clear=True)
+
+    projections = None
+    if world == 1 and not args.no_projections:
+        del chain
+        torch.cuda.empty_cache()
+        chain = None
+        projections = bench_projections(torch, peak, quick=args.quick)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_oracle_tok_s(10.0 if not args.quick else 3.0)
+
+    if rank == 0:
+        value = args.steps / step_s
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(step_s * 1000.0 / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,0.02^2) bf16 weights, N(0,1) bf16 token)",
+            "config": {"workload": "c5_chain_llama3_8b_shapes_32_layers_m1", "layers": shape.layers, "M": 1,
+                       "hidden": shape.hidden, "ffn": shape.ffn, "kv": shape.kv,
+                       "parallelism": f"column-shard x{world}" + (" + nccl all-gather" if world > 1 else ""),
+                       "bytes_per_token": shape.bytes_per_token(),
+                       "l2": "weights 13.96 GB per step >> 126 MB L2 (no flush needed)",
+                       "graph": "one CUDA graph per token step, PDL launches"},
+            "gpu_launches": args.steps * 7 * shape.layers,
+            "hbm_gbs_per_gpu": round(shape.bytes_per_token() / world * value / 1e9, 1),
+            "roofline": roofline,
+            "e2e": {"value": round(e2e_steps / e2e_s, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": int(x_host.numel() * x_host.element_size()),
+                    "d2h_bytes_per_step": int(y_host.numel() * y_host.element_size())},
+            "clocks": clocks, "output_sha256": digest, "device_status": status,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        if projections is not None:
+            line["projections"] = projections
+        print(json.dumps(line), flush=True)
+
+    if chain is not None:
+        chain.release()
+    if world > 1:
+        import torch.distributed as dist
+
+        barrier(world)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,208 @@
+/* klab_b200: C ABI of the B200-native small-batch projection path.
+ *
+ * Plain pointers, sizes and a CUDA stream handle; no C++ or framework types.
+ * All device pointers are caller-owned; every call enqueues asynchronously on
+ * `stream` (a cudaStream_t, NULL = legacy default stream) of the current CUDA
+ * device and never synchronizes. Return value: 0 on success, a positive
+ * cudaError_t, or a negative KLAB_E* code below. Output layout is
+ * out[t * ldo + row] for token t and output row `row` (ldo = N for a dense
+ * [M, N] result; a larger ldo writes into a column slice of a wider buffer).
+ *
+ * Numerics (every projection): FP32 accumulation with fma.rn, a fixed
+ * reduction order that depends only on K and the weight format, and one final
+ * cvt.rn.bf16.f32 for BF16 outputs. Coded (lossless) BF16 weights give
+ * bit-identical results to the same weights stored raw; any subset of output
+ * rows (a column shard) gives bit-identical values to the full projection.
+ *
+ * Workspace: projections may split K across thread blocks when N is small.
+ * That needs `workspace` of klab_gemv_workspace_bytes(...) bytes, zero-filled
+ * once before first use and then left alone (every launch leaves it zeroed).
+ * Pass NULL / 0 to disable splitting; results are identical either way. One
+ * workspace must not be used by launches that can run concurrently.
+ */
+#ifndef KLAB_B200_H
+#define KLAB_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KLAB_API __attribute__((visibility("default")))
+#else
+#define KLAB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- codes */
+
+/* Element types of activations and outputs. */
+#define KLAB_DT_BF16 0
+#define KLAB_DT_F16 1
+#define KLAB_DT_F32 2
+
+/* Weight formats (klab_gemv wfmt). */
+#define KLAB_W_BF16 0      /* BF16 [N,K] */
+#define KLAB_W_F16 1       /* FP16 [N,K] */
+#define KLAB_W_F32 2       /* FP32 [N,K] */
+#define KLAB_W_CBF16 3     /* lossless BF16 codec v1: payload u8 + metadata u32 [N*ceil(K/64)] */
+#define KLAB_W_I8_ROW 4    /* int8 [N,K] + fp32 scale [N] */
+#define KLAB_W_I8_G64 5    /* int8 [N,K] + fp32 scale [N,K/64] */
+#define KLAB_W_FP4_G32H 6  /* E2M1 [N,K/2] (low nibble = even k) + fp16 scale [N,K/32] */
+#define KLAB_W_FP4_G16E 7  /* E2M1 [N,K/2] + E4M3 scale [N,K/16] + fp32 global scale */
+
+/* FP4 scale kinds (klab_fp4_linear / klab_fp4_dequantize). */
+#define KLAB_FP4_E4M3_G16 0
+#define KLAB_FP4_F16_G32 1
+
+/* L2 prefetch kinds (klab_l2_prefetch). */
+#define KLAB_L2_HINT 0
+#define KLAB_L2_HINT_LAST 1
+#define KLAB_L2_LOAD 2
+
+/* Error codes. -1000..-1002 keep the meaning of the reference driver ABI. */
+#define KLAB_E_DRIVER (-1000)      /* CUDA driver or a required symbol not loadable */
+#define KLAB_E_NO_CONTEXT (-1001)  /* no current CUDA context */
+#define KLAB_E_INVALID (-1002)     /* null argument or zero/negative dimension */
+#define KLAB_E_SHAPE (-2001)       /* shape not supported by this format */
+#define KLAB_E_ALIGN (-2002)       /* pointer/stride alignment not supported */
+#define KLAB_E_UNSUPPORTED (-2003) /* dtype/format combination not supported */
+#define KLAB_E_DEVICE (-2004)      /* a kernel recorded a device-side error (bounded wait expired) */
+
+/* Options (klab_set_option). */
+#define KLAB_OPT_PDL 0        /* 1 (default): launch with programmatic dependent launch */
+#define KLAB_OPT_SPLIT 1      /* -1 (default) automatic, 0 never, 1 always (when workspace allows) */
+#define KLAB_OPT_GENERIC 2    /* 1: force the cooperative-load (non bulk-copy) fill path */
+
+/* ---------------------------------------------------------------- projections */
+
+/* Generic projection: out = x[M,K] . W^T for any weight format.
+ * Replaces the per-format launches of the reference wrappers:
+ *   compressed_bf16.py:421-460 (_coded, raw_linear), mtile_bf16.py:150-188 (_launch),
+ *   int8_weights.py:38-67, fp4.py:63-97, half_projection.py:24-50,
+ *   kernel_lab.py:197-279 (matmul / warp_matmul / tiled_matmul).
+ * aux: coded metadata, or scales (per wfmt); gscale: device pointer (FP4_G16E only). */
+KLAB_API int klab_gemv(int wfmt, int xdtype, const void* x, int ldx, const void* w, const void* aux,
+              const float* gscale, void* out, int ldo, int out_dtype, int m, int n, int k,
+              void* workspace, size_t workspace_bytes, void* stream);
+
+/* BF16 x, raw BF16 W, BF16 or FP32 out.
+ * Replaces compressed_bf16.raw_linear (compressed_bf16.py:450-460, kernels
+ * cbf16_raw_{bf16,fp32}_t*_v*, compressed_kernels.cu:156-176) and
+ * mtile_bf16.raw_linear (mtile_bf16.py:177-188, mtbf16_raw_*, mtile_kernels.cu:122-144). */
+KLAB_API int klab_raw_linear(const void* x, const void* w, void* out, int out_dtype, int m, int n, int k,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* BF16 x, lossless-coded BF16 W (payload 32-byte aligned, K % 64 == 0).
+ * Replaces compressed_bf16._coded / fused_linear (compressed_bf16.py:421-447,
+ * cbf16_coded_*) and mtile_bf16.fused_linear (mtile_bf16.py:161-174, mtbf16_coded_*). */
+KLAB_API int klab_coded_linear(const void* x, const void* payload, const uint32_t* metadata, void* out,
+                      int out_dtype, int m, int n, int k, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
+/* x and W both FP16 or both BF16 (dtype), FP32 out.
+ * Replaces half_projection.fused_linear (half_projection.py:24-50, half_warp_*,
+ * half_kernels.cu:63-80). */
+KLAB_API int klab_half_linear(const void* x, const void* w, int dtype, float* out, int m, int n, int k,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* FP32 x, FP32 W, FP32 out.
+ * Replaces KernelLab.matmul / warp_matmul / tiled_matmul / tiny_matmul
+ * (kernel_lab.py:197-294, kernels.cu:13-166, adaptive_kernels.cu:3-41,
+ * projection_kernels.cu:17-89). */
+KLAB_API int klab_f32_linear(const float* x, const float* w, float* out, int m, int n, int k, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* int8 W with fp32 scales: group 64 -> scales [N,K/64] (reference format,
+ * int8_weights.py:23-35), group 0 -> scales [N] (per-row). x BF16/FP16/FP32.
+ * Replaces int8_weights.fused_linear (int8_weights.py:38-67, int8_a{16,32}_t*,
+ * int8_kernels.cu:28-34). */
+KLAB_API int klab_int8_linear(const void* x, int xdtype, const int8_t* codes, const float* scales, int group,
+                     void* out, int out_dtype, int m, int n, int k, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* E2M1 W, two per byte (low nibble = even k). scale_kind KLAB_FP4_E4M3_G16:
+ * scales [N,K/16] E4M3 bytes and `gscale` one fp32 (reference format,
+ * fp4.py:33-60); KLAB_FP4_F16_G32: scales [N,K/32] fp16, gscale unused.
+ * Replaces fp4.fused_linear (fp4.py:63-97, fp4_a{16,32}_t*, fp4_kernels.cu:56-63). */
+KLAB_API int klab_fp4_linear(const void* x, int xdtype, const uint8_t* packed, const void* scales,
+                    int scale_kind, const float* gscale, void* out, int out_dtype, int m, int n, int k,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Workspace bytes a klab_gemv call of this shape can use for split-K (0 = none). */
+KLAB_API size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k);
+
+/* ---------------------------------------------------------------- decode */
+
+/* Lossless BF16 codec v1 -> original uint16 bits [N,K] (any K).
+ * Replaces compressed_bf16.unpack_weights (compressed_bf16.py:463-473,
+ * cbf16_unpack, compressed_kernels.cu:181-200). */
+KLAB_API int klab_cbf16_unpack(const void* payload, const uint32_t* metadata, uint16_t* out, int n, int k,
+                      void* stream);
+
+/* int8 -> fp32 [N,K] = code * scale (group 64 or 0 = per row).
+ * Replaces Int8Weights.dequantize (int8_weights.py:15-17). */
+KLAB_API int klab_int8_dequantize(const int8_t* codes, const float* scales, int group, float* out, int n, int k,
+                         void* stream);
+
+/* E2M1 -> fp32 [N,K]; E4M3/16: e2m1 * (scale * gscale) (fp4.py:21-27); F16/32: e2m1 * scale.
+ * Replaces FP4Weights.dequantize (fp4.py:21-27). */
+KLAB_API int klab_fp4_dequantize(const uint8_t* packed, const void* scales, int scale_kind, const float* gscale,
+                        float* out, int n, int k, void* stream);
+
+/* Host-side codec (CPU, preparation time). Pack: writes N*ceil(K/64) metadata
+ * words and sets *payload_bytes; writes the payload when `payload` is non-NULL
+ * and payload_capacity is large enough (a NULL payload is a size query).
+ * Replaces compressed_bf16.pack_bits (compressed_bf16.py:99-151). */
+KLAB_API int klab_cbf16_pack_host(const uint16_t* bits, int n, int k, uint32_t* metadata, uint8_t* payload,
+                                  size_t payload_capacity, size_t* payload_bytes);
+/* Validated decode to [N,K] bits: canonical offsets, raw-block base zero,
+ * exponent range and tail padding; KLAB_E_INVALID on malformed input.
+ * Replaces the checks and decode of compressed_bf16._decoded_chunks / unpack_bits
+ * (compressed_bf16.py:162-243). */
+KLAB_API int klab_cbf16_unpack_host(const uint8_t* payload, size_t payload_bytes, const uint32_t* metadata, int n,
+                                    int k, uint16_t* out);
+
+/* ---------------------------------------------------------------- L2 prefetch */
+
+/* Side-stream prefetch of [p, p + bytes) into L2 with `blocks` x `threads`
+ * threads, one request per `stride` bytes; never writes. sink: a device word
+ * (never written in practice). Replaces l2prefetch.prefetch
+ * (research/l2-prefetch/src/l2prefetch.py:27-35; kernels l2_hint / l2_hint_last /
+ * l2_load, prefetch_kernels.cu:3-25). */
+KLAB_API int klab_l2_prefetch(const void* p, long long bytes, int blocks, int threads, int stride, int kind,
+                     unsigned* sink, void* stream);
+
+/* ---------------------------------------------------------------- control */
+
+KLAB_API int klab_set_option(int option, int value);
+KLAB_API int klab_get_option(int option);
+/* Read the current device's status word (0 = no device-side error); clear it when clear != 0. */
+KLAB_API int klab_device_status(int clear);
+KLAB_API const char* klab_error_string(int code);
+KLAB_API int klab_version(void);
+
+/* ---------------------------------------------------------------- driver ABI
+ * The reference's C ABI over the CUDA driver (native/driver.cpp:46-90), same
+ * signatures, error codes and threading: load an image (PTX, cubin or fatbin)
+ * into the current context, look up a kernel, launch it on a stream. */
+KLAB_API int lab_load_ptx(const char* image, void** module_out);                                 /* driver.cpp:46-57 */
+KLAB_API int lab_get_kernel(void* module, const char* name, void** fn_out);                     /* driver.cpp:59-63 */
+KLAB_API int lab_launch(void* fn, unsigned grid_x, unsigned grid_y, unsigned block_x, void* stream,
+               void** args);                                                           /* driver.cpp:65-71 */
+KLAB_API int lab_unload(void* module);                                                          /* driver.cpp:73-77 */
+KLAB_API const char* lab_error_string(int code);                                                /* driver.cpp:79-90 */
+/* Extension (no reference counterpart): dynamic shared memory and flags
+ * (bit 0: programmatic dependent launch) for bulk-copy ring kernels. */
+KLAB_API int lab_launch_ex(void* fn, unsigned grid_x, unsigned grid_y, unsigned block_x, unsigned smem_bytes,
+                  unsigned flags, void* stream, void** args);
+/* Load an image from a file path (cubins shipped beside the library). */
+KLAB_API int lab_load_file(const char* path, void** module_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KLAB_B200_H */

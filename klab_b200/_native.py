@@ -1,0 +1,190 @@
+"""ctypes binding of libklab_b200.so (include/klab_b200.h).
+
+The reference drives its native layer through ctypes too (kernel_lab.py:120-130,
+cuda_module.py:149-158). There is no fallback: importing an operator module on
+a machine without the built library raises immediately, and every projection
+runs the sm_100a kernels of this library.
+"""
+
+from __future__ import annotations
+
+import ctypes as ct
+import threading
+from pathlib import Path
+
+LIB_DIR = Path(__file__).resolve().parent / "_lib"
+LIB_PATH = LIB_DIR / "libklab_b200.so"
+PREFETCH_CUBIN = LIB_DIR / "prefetch_kernels.cubin"
+
+# include/klab_b200.h constants
+DT_BF16, DT_F16, DT_F32 = 0, 1, 2
+W_BF16, W_F16, W_F32, W_CBF16, W_I8_ROW, W_I8_G64, W_FP4_G32H, W_FP4_G16E = range(8)
+FP4_E4M3_G16, FP4_F16_G32 = 0, 1
+L2_HINT, L2_HINT_LAST, L2_LOAD = 0, 1, 2
+OPT_PDL, OPT_SPLIT, OPT_GENERIC = 0, 1, 2
+E_DRIVER, E_NO_CONTEXT, E_INVALID = -1000, -1001, -1002
+E_SHAPE, E_ALIGN, E_UNSUPPORTED, E_DEVICE = -2001, -2002, -2003, -2004
+
+_P = ct.c_void_p
+_I = ct.c_int
+_SZ = ct.c_size_t
+_SIGNATURES = {
+    "klab_gemv": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_raw_linear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_coded_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_half_linear": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _SZ, _P]),
+    "klab_f32_linear": (_I, [_P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
+    "klab_int8_linear": (_I, [_P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_fp4_linear": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_gemv_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "klab_cbf16_unpack": (_I, [_P, _P, _P, _I, _I, _P]),
+    "klab_int8_dequantize": (_I, [_P, _P, _I, _P, _I, _I, _P]),
+    "klab_fp4_dequantize": (_I, [_P, _P, _I, _P, _P, _I, _I, _P]),
+    "klab_cbf16_pack_host": (_I, [_P, _I, _I, _P, _P, _SZ, ct.POINTER(_SZ)]),
+    "klab_cbf16_unpack_host": (_I, [_P, _SZ, _P, _I, _I, _P]),
+    "klab_l2_prefetch": (_I, [_P, ct.c_longlong, _I, _I, _I, _I, _P, _P]),
+    "klab_set_option": (_I, [_I, _I]),
+    "klab_get_option": (_I, [_I]),
+    "klab_device_status": (_I, [_I]),
+    "klab_error_string": (ct.c_char_p, [_I]),
+    "klab_version": (_I, []),
+    "lab_load_ptx": (_I, [ct.c_char_p, ct.POINTER(_P)]),
+    "lab_load_file": (_I, [ct.c_char_p, ct.POINTER(_P)]),
+    "lab_get_kernel": (_I, [_P, ct.c_char_p, ct.POINTER(_P)]),
+    "lab_launch": (_I, [_P, ct.c_uint, ct.c_uint, ct.c_uint, _P, ct.POINTER(_P)]),
+    "lab_launch_ex": (_I, [_P, ct.c_uint, ct.c_uint, ct.c_uint, ct.c_uint, ct.c_uint, _P, ct.POINTER(_P)]),
+    "lab_unload": (_I, [_P]),
+    "lab_error_string": (ct.c_char_p, [_I]),
+}
+EXPORTED = tuple(_SIGNATURES)
+
+_lib = None
+_lock = threading.Lock()
+
+
+class KlabError(RuntimeError):
+    """A native call failed; .code is the klab / CUDA error code."""
+
+    def __init__(self, code, what):
+        self.code = code
+        super().__init__(f"{what} failed ({code}): {error_string(code)}")
+
+
+def lib():
+    """The loaded library. Raises when it has not been built (no fallback)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m klab_b200.build` "
+                                       "(klab_b200 has no CPU or framework fallback)")
+                handle = ct.CDLL(str(LIB_PATH))
+                for name, (restype, argtypes) in _SIGNATURES.items():
+                    fn = getattr(handle, name)
+                    fn.restype, fn.argtypes = restype, argtypes
+                _lib = handle
+    return _lib
+
+
+def error_string(code: int) -> str:
+    text = lib().klab_error_string(int(code))
+    return text.decode() if text else "unknown error"
+
+
+def check(code: int, what: str) -> None:
+    if code:
+        raise KlabError(code, what)
+
+
+def ptr(tensor) -> int:
+    return tensor.data_ptr()
+
+
+def current_stream(device):
+    import torch
+
+    return torch.cuda.current_stream(device)
+
+
+def record(stream, *tensors):
+    """ctypes launches bypass the caching allocator's stream bookkeeping
+    (kernel_lab.py:183-186); tell it which stream used each tensor."""
+    import torch
+
+    if torch.cuda.is_current_stream_capturing():
+        return
+    for t in tensors:
+        if t is not None:
+            t.record_stream(stream)
+
+
+class _Workspaces:
+    """Per (device, stream) split-K workspace: zero-filled once, grown outside
+    graph capture, then reused by every launch on that stream (launches leave
+    it zeroed)."""
+
+    def __init__(self):
+        self._buffers = {}
+        self._lock = threading.Lock()
+
+    def get(self, device_index: int, stream, need: int):
+        import torch
+
+        if need <= 0:
+            return None
+        key = (device_index, int(stream.cuda_stream))
+        with self._lock:
+            buf = self._buffers.get(key)
+            if buf is not None and buf.numel() >= need:
+                return buf
+            if torch.cuda.is_current_stream_capturing():
+                return buf if buf is not None and buf.numel() >= need else None
+            size = max(need, 1 << 20)
+            buf = torch.zeros(size, dtype=torch.uint8, device=torch.device("cuda", device_index))
+            self._buffers[key] = buf
+            return buf
+
+
+WORKSPACES = _Workspaces()
+
+
+def workspace_for(wfmt: int, m: int, n: int, k: int, device_index: int, stream):
+    need = lib().klab_gemv_workspace_bytes(wfmt, m, n, k)
+    buf = WORKSPACES.get(device_index, stream, int(need))
+    if buf is None:
+        return None, 0
+    return buf.data_ptr(), buf.numel()
+
+
+def set_option(option: int, value: int) -> None:
+    check(lib().klab_set_option(option, value), "klab_set_option")
+
+
+def get_option(option: int) -> int:
+    return lib().klab_get_option(option)
+
+
+def device_status(clear: bool = True) -> int:
+    """The current device's status word (0: no kernel gave up a bounded wait)."""
+    value = lib().klab_device_status(1 if clear else 0)
+    if value < 0 or value > 16:
+        raise KlabError(value, "klab_device_status")
+    return value
+
+
+def gemv(wfmt, xdt, x, w, aux, gscale, out, out_dt, m, n, k, *, ldx=None, ldo=None, workspace=True):
+    """Launch one projection on torch's current stream of x's device."""
+    import torch
+
+    device = x.device
+    stream = torch.cuda.current_stream(device)
+    ws_ptr, ws_bytes = (workspace_for(wfmt, m, n, k, device.index, stream) if workspace else (None, 0))
+    with torch.cuda.device(device):
+        rc = lib().klab_gemv(wfmt, xdt, x.data_ptr(), k if ldx is None else ldx, w.data_ptr(),
+                             None if aux is None else aux.data_ptr(),
+                             None if gscale is None else gscale.data_ptr(), out.data_ptr(),
+                             n if ldo is None else ldo, out_dt, m, n, k, ws_ptr, ws_bytes, stream.cuda_stream)
+    check(rc, "klab_gemv")
+    record(stream, x, w, aux, gscale, out)
+    return out

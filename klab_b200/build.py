@@ -1,0 +1,112 @@
+"""Build recipe for libklab_b200.so (sm_100a) and the standalone prefetch cubin.
+
+Runs nvcc directly (no JIT, no torch extension machinery) and writes everything
+in-tree under klab_b200/_lib/, so the built files travel with the repository
+snapshot. Objects are rebuilt only when a source or header is newer.
+
+    python -m klab_b200.build            # build (incremental)
+    python -m klab_b200.build --clean    # rebuild everything
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+CSRC = HERE / "csrc"
+INCLUDE = HERE.parent / "include"
+OUT = HERE / "_lib"
+OBJ = OUT / "obj"
+LIBRARY = OUT / "libklab_b200.so"
+ALIAS = OUT / "libkernel_lab.so"  # the reference's library name (native/build/libkernel_lab.so)
+PREFETCH_CUBIN = OUT / "prefetch_kernels.cubin"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
+                     "-fvisibility=hidden", f"-I{INCLUDE}"]
+CUDA_SOURCES = ("capi.cu", "aux_kernels.cu", "prefetch_kernels.cu", "gemv_half.cu", "gemv_cbf16.cu",
+                "gemv_int8.cu", "gemv_fp4a.cu", "gemv_fp4b.cu")
+CXX_SOURCES = ("driver_abi.cpp", "codec_host.cpp")
+EXPORTS = OUT / "exports.map"
+
+
+def nvcc() -> str:
+    for candidate in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if candidate and Path(candidate).exists():
+            return candidate
+    raise RuntimeError("nvcc not found; klab_b200 builds with the CUDA toolkit's nvcc")
+
+
+def _headers():
+    return list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list(INCLUDE.glob("*.h"))
+
+
+def _stale(target: Path, sources) -> bool:
+    if not target.exists():
+        return True
+    mtime = target.stat().st_mtime
+    return any(Path(s).stat().st_mtime > mtime for s in sources)
+
+
+def _run(cmd):
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode:
+        raise RuntimeError(f"command failed ({result.returncode}): {' '.join(map(str, cmd))}\n"
+                           f"{result.stdout}\n{result.stderr}")
+    return result
+
+
+def _compile(source: Path, headers, verbose=False) -> Path:
+    obj = OBJ / (source.name + ".o")
+    if _stale(obj, [source, *headers]):
+        if source.suffix == ".cu":
+            cmd = [nvcc(), *NVCC_FLAGS, "-c", str(source), "-o", str(obj)]
+            if verbose:
+                cmd.insert(1, "-Xptxas=-v")
+        else:
+            cmd = [nvcc(), "-std=c++17", "-O2", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+                   f"-I{INCLUDE}", "-c", str(source), "-o", str(obj)]
+        result = _run(cmd)
+        if verbose and result.stderr:
+            print(result.stderr, file=sys.stderr)
+    return obj
+
+
+def build(clean: bool = False, verbose: bool = False) -> Path:
+    """Compile every kernel for sm_100a and link libklab_b200.so; return its path."""
+    if clean and OUT.exists():
+        shutil.rmtree(OUT)
+    OBJ.mkdir(parents=True, exist_ok=True)
+    headers = _headers()
+    sources = [CSRC / s for s in CUDA_SOURCES] + [CSRC / s for s in CXX_SOURCES]
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
+        objects = list(pool.map(lambda s: _compile(s, headers, verbose), sources))
+    EXPORTS.write_text("{ global: klab_*; lab_*; local: *; };\n")
+    if _stale(LIBRARY, objects + [EXPORTS]):
+        _run([nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIBRARY), *map(str, objects),
+              "-Xlinker", f"--version-script={EXPORTS}", "-ldl"])
+    if _stale(PREFETCH_CUBIN, [CSRC / "prefetch_kernels.cu", *headers]):
+        _run([nvcc(), *ARCH, "-lineinfo", "-O3", "-std=c++17", f"-I{INCLUDE}", "-cubin",
+              str(CSRC / "prefetch_kernels.cu"), "-o", str(PREFETCH_CUBIN)])
+    if ALIAS.is_symlink() or ALIAS.exists():
+        ALIAS.unlink()
+    ALIAS.symlink_to(LIBRARY.name)
+    return LIBRARY
+
+
+def main(argv=None):
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    parser.add_argument("--clean", action="store_true")
+    parser.add_argument("--verbose", action="store_true", help="print ptxas register/spill reports")
+    args = parser.parse_args(argv)
+    print(build(clean=args.clean, verbose=args.verbose))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,417 @@
+// C ABI entry points of libklab_b200.so (declared in include/klab_b200.h):
+// argument validation, launch planning for the streaming projection kernel,
+// options and the per-device status word.
+#include <atomic>
+#include <cstdint>
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "gemv_launch.cuh"
+#include "klab_kernels.h"
+
+namespace klab {
+
+// Device status word: kernels that give up a bounded wait record a code here.
+__device__ int g_status_word;
+
+namespace {
+
+constexpr size_t kXSmemCap = 96 * 1024;       // FP32 x staging budget per CTA
+constexpr size_t kMaxSmem = 227 * 1024;
+
+std::atomic<int> g_opt_pdl{1};
+std::atomic<int> g_opt_split{-1};
+std::atomic<int> g_opt_generic{0};
+
+struct DeviceInfo {
+  bool ready = false;
+  int sms = 0;
+  int* status = nullptr;
+};
+
+std::mutex g_mutex;
+DeviceInfo g_devices[64];
+std::map<std::tuple<int, int, int, int, int, size_t>, int> g_occupancy;
+
+int current_device_info(DeviceInfo** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (dev < 0 || dev >= 64) return KLAB_E_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  DeviceInfo& info = g_devices[dev];
+  if (!info.ready) {
+    err = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (err != cudaSuccess) return err;
+    // The host-side name of a __device__ variable is not its device address;
+    // ask the runtime for this device's address once.
+    err = cudaGetSymbolAddress(reinterpret_cast<void**>(&info.status), g_status_word);
+    if (err != cudaSuccess) return err;
+    info.ready = true;
+  }
+  *out = &info;
+  return 0;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int dtype_bytes(int dt) { return dt == KLAB_DT_F32 ? 4 : 2; }
+
+int vals_of(int wfmt) {
+  switch (wfmt) {
+    case W_F32: return 4;
+    case W_I8_ROW:
+    case W_I8_G64: return 16;
+    case W_FP4_G32H:
+    case W_FP4_G16E: return 32;
+    default: return 8;
+  }
+}
+
+size_t warp_region_bytes(int wfmt) {
+  switch (wfmt) {
+    case W_BF16: return Layout<W_BF16>::WARP_BYTES;
+    case W_F16: return Layout<W_F16>::WARP_BYTES;
+    case W_F32: return Layout<W_F32>::WARP_BYTES;
+    case W_CBF16: return Layout<W_CBF16>::WARP_BYTES;
+    case W_I8_ROW: return Layout<W_I8_ROW>::WARP_BYTES;
+    case W_I8_G64: return Layout<W_I8_G64>::WARP_BYTES;
+    case W_FP4_G32H: return Layout<W_FP4_G32H>::WARP_BYTES;
+    default: return Layout<W_FP4_G16E>::WARP_BYTES;
+  }
+}
+
+size_t bar_region_bytes(int wfmt) {
+  const int bars = kDepth + (wfmt == W_CBF16 ? kMetaRing : 0);
+  return ((static_cast<size_t>(kWarps) * bars * 8 + 127) / 128) * 128;
+}
+
+int tile_for(int m) { return m == 1 ? 1 : m == 2 ? 2 : m <= 4 ? 4 : 8; }
+
+cudaError_t run_family(int wfmt, const GemvParams& p, const LaunchShape& s, cudaStream_t stream, int* occ) {
+  switch (wfmt) {
+    case W_BF16:
+    case W_F16:
+    case W_F32: return gemv_run_half(wfmt, p, s, stream, occ);
+    case W_CBF16: return gemv_run_cbf16(wfmt, p, s, stream, occ);
+    case W_I8_ROW:
+    case W_I8_G64: return gemv_run_int8(wfmt, p, s, stream, occ);
+    case W_FP4_G32H: return gemv_run_fp4a(wfmt, p, s, stream, occ);
+    case W_FP4_G16E: return gemv_run_fp4b(wfmt, p, s, stream, occ);
+    default: return cudaErrorNotSupported;
+  }
+}
+
+int occupancy(int wfmt, const LaunchShape& s) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(dev, wfmt, s.xfmt * 16 + s.xmode, s.mt, 0, s.smem);
+  {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_occupancy.find(key);
+    if (it != g_occupancy.end()) return it->second;
+  }
+  int occ = 0;
+  GemvParams dummy = {};
+  if (run_family(wfmt, dummy, s, nullptr, &occ) != cudaSuccess) occ = 0;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  g_occupancy[key] = occ;
+  return occ;
+}
+
+bool tma_eligible(int wfmt, const void* w, const void* aux, int k) {
+  switch (wfmt) {
+    case W_BF16:
+    case W_F16: return aligned16(w) && k % 8 == 0;
+    case W_F32: return aligned16(w) && k % 4 == 0;
+    case W_I8_ROW: return aligned16(w) && k % 16 == 0;
+    case W_CBF16:
+    case W_I8_G64:
+    case W_FP4_G32H:
+    case W_FP4_G16E: return aligned16(w) && aligned16(aux) && k % 256 == 0;
+    default: return false;
+  }
+}
+
+bool x_compatible(int wfmt, int xdt) {
+  switch (wfmt) {
+    case W_BF16:
+    case W_CBF16: return xdt == KLAB_DT_BF16;
+    case W_F16: return xdt == KLAB_DT_F16;
+    case W_F32: return xdt == KLAB_DT_F32;
+    default: return xdt == KLAB_DT_BF16 || xdt == KLAB_DT_F16 || xdt == KLAB_DT_F32;
+  }
+}
+
+int shape_ok(int wfmt, int k) {
+  switch (wfmt) {
+    case W_CBF16:
+    case W_I8_G64: return k % 64 == 0;
+    case W_FP4_G32H: return k % 32 == 0;
+    case W_FP4_G16E: return k % 16 == 0;
+    default: return 1;
+  }
+}
+
+size_t workspace_need(int tiles, int mt, int n, int chunks) {
+  const size_t tickets = ((static_cast<size_t>(tiles) * n * 4 + 255) / 256) * 256;
+  return tickets + static_cast<size_t>(tiles) * mt * n * chunks * 4;
+}
+
+int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const void* aux, const float* gscale,
+             void* out, int ldo, int out_dt, int m, int n, int k, void* ws, size_t ws_bytes, void* stream) {
+  if (!x || !w || !out) return KLAB_E_INVALID;
+  if (m <= 0 || n <= 0 || k <= 0 || ldx < k || ldo < n) return KLAB_E_INVALID;
+  if (wfmt < W_BF16 || wfmt > W_FP4_G16E) return KLAB_E_UNSUPPORTED;
+  if (!x_compatible(wfmt, xdt)) return KLAB_E_UNSUPPORTED;
+  if (out_dt != KLAB_DT_BF16 && out_dt != KLAB_DT_F32) return KLAB_E_UNSUPPORTED;
+  const bool needs_aux = wfmt >= W_CBF16;
+  if (needs_aux && !aux) return KLAB_E_INVALID;
+  if (wfmt == W_FP4_G16E && !gscale) return KLAB_E_INVALID;
+  if (!shape_ok(wfmt, k)) return KLAB_E_SHAPE;
+
+  DeviceInfo* info = nullptr;
+  int rc = current_device_info(&info);
+  if (rc) return rc;
+
+  const int vals = vals_of(wfmt);
+  const int kc = 256 * vals;
+  const int chunks = (k + kc - 1) / kc;
+  const int seg_cols = 32 * vals;
+  const long long kpad = ((static_cast<long long>(k) + seg_cols - 1) / seg_cols) * seg_cols;
+  const int xb = dtype_bytes(xdt);
+  const bool x_global_ok =
+      aligned16(x) && (static_cast<long long>(ldx) * xb) % 16 == 0 && k % vals == 0;
+
+  int mt = tile_for(m);
+  int xmode = XM_SMEM;
+  for (;;) {
+    if (static_cast<size_t>(mt) * kpad * 4 <= kXSmemCap) {
+      xmode = XM_SMEM;
+      break;
+    }
+    if (x_global_ok) {
+      xmode = XM_GLOBAL;
+      break;
+    }
+    if (mt == 1) return KLAB_E_SHAPE;
+    mt /= 2;
+  }
+  const int tiles = (m + mt - 1) / mt;
+  if (tiles > 65535) return KLAB_E_SHAPE;
+
+  LaunchShape s = {};
+  s.xfmt = xdt;
+  s.xmode = xmode;
+  s.mt = mt;
+  s.pdl = g_opt_pdl.load() != 0;
+  s.smem = bar_region_bytes(wfmt) + kWarps * warp_region_bytes(wfmt) +
+           (xmode == XM_SMEM ? static_cast<size_t>(mt) * kpad * 4 : 0);
+  if (s.smem > kMaxSmem) return KLAB_E_SHAPE;
+  const int occ = occupancy(wfmt, s);
+  if (occ <= 0) return KLAB_E_UNSUPPORTED;
+  const int gmax = occ * info->sms / tiles > 0 ? occ * info->sms / tiles : 1;
+
+  GemvParams p = {};
+  p.x = x;
+  p.w = w;
+  p.aux = aux;
+  p.gscale = gscale;
+  p.out = out;
+  p.status = info->status;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.ldx = ldx;
+  p.ldo = ldo;
+  p.out_f32 = out_dt == KLAB_DT_F32;
+  p.chunks = chunks;
+  p.use_tma = (g_opt_generic.load() == 0) && tma_eligible(wfmt, w, aux, k);
+
+  const size_t need = workspace_need(tiles, mt, n, chunks);
+  const bool can_split = ws && ws_bytes >= need && chunks >= 2 && aligned16(ws);
+  const int opt = g_opt_split.load();
+  const bool split = can_split && (opt == 1 || (opt == -1 && chunks >= 3 &&
+                                                static_cast<long long>(n) * 2 < static_cast<long long>(gmax) * kWarps));
+  int grid_x;
+  if (split) {
+    const long long items = static_cast<long long>(n) * chunks;
+    const long long want = (items + kWarps - 1) / kWarps;
+    grid_x = static_cast<int>(want < gmax ? want : gmax);
+    p.split = 1;
+    p.tickets = static_cast<unsigned*>(ws);
+    p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + ((static_cast<size_t>(tiles) * n * 4 + 255) / 256) * 256);
+  } else {
+    grid_x = n < gmax ? n : gmax;
+    p.split = 0;
+  }
+  s.grid = dim3(grid_x, tiles, 1);
+  return run_family(wfmt, p, s, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+}  // namespace
+}  // namespace klab
+
+using namespace klab;
+
+extern "C" {
+
+int klab_gemv(int wfmt, int xdtype, const void* x, int ldx, const void* w, const void* aux, const float* gscale,
+              void* out, int ldo, int out_dtype, int m, int n, int k, void* workspace, size_t workspace_bytes,
+              void* stream) {
+  return run_gemv(wfmt, xdtype, x, ldx, w, aux, gscale, out, ldo, out_dtype, m, n, k, workspace, workspace_bytes,
+                  stream);
+}
+
+int klab_raw_linear(const void* x, const void* w, void* out, int out_dtype, int m, int n, int k, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  return run_gemv(W_BF16, KLAB_DT_BF16, x, k, w, nullptr, nullptr, out, n, out_dtype, m, n, k, workspace,
+                  workspace_bytes, stream);
+}
+
+int klab_coded_linear(const void* x, const void* payload, const uint32_t* metadata, void* out, int out_dtype, int m,
+                      int n, int k, void* workspace, size_t workspace_bytes, void* stream) {
+  if (payload && (reinterpret_cast<uintptr_t>(payload) & 31u)) return KLAB_E_ALIGN;
+  return run_gemv(W_CBF16, KLAB_DT_BF16, x, k, payload, metadata, nullptr, out, n, out_dtype, m, n, k, workspace,
+                  workspace_bytes, stream);
+}
+
+int klab_half_linear(const void* x, const void* w, int dtype, float* out, int m, int n, int k, void* workspace,
+                     size_t workspace_bytes, void* stream) {
+  if (dtype != KLAB_DT_BF16 && dtype != KLAB_DT_F16) return KLAB_E_UNSUPPORTED;
+  return run_gemv(dtype == KLAB_DT_BF16 ? W_BF16 : W_F16, dtype, x, k, w, nullptr, nullptr, out, n, KLAB_DT_F32, m,
+                  n, k, workspace, workspace_bytes, stream);
+}
+
+int klab_f32_linear(const float* x, const float* w, float* out, int m, int n, int k, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  return run_gemv(W_F32, KLAB_DT_F32, x, k, w, nullptr, nullptr, out, n, KLAB_DT_F32, m, n, k, workspace,
+                  workspace_bytes, stream);
+}
+
+int klab_int8_linear(const void* x, int xdtype, const int8_t* codes, const float* scales, int group, void* out,
+                     int out_dtype, int m, int n, int k, void* workspace, size_t workspace_bytes, void* stream) {
+  if (group != 0 && group != 64) return KLAB_E_UNSUPPORTED;
+  return run_gemv(group ? W_I8_G64 : W_I8_ROW, xdtype, x, k, codes, scales, nullptr, out, n, out_dtype, m, n, k,
+                  workspace, workspace_bytes, stream);
+}
+
+int klab_fp4_linear(const void* x, int xdtype, const uint8_t* packed, const void* scales, int scale_kind,
+                    const float* gscale, void* out, int out_dtype, int m, int n, int k, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  int wfmt;
+  if (scale_kind == KLAB_FP4_E4M3_G16)
+    wfmt = W_FP4_G16E;
+  else if (scale_kind == KLAB_FP4_F16_G32)
+    wfmt = W_FP4_G32H;
+  else
+    return KLAB_E_UNSUPPORTED;
+  return run_gemv(wfmt, xdtype, x, k, packed, scales, gscale, out, n, out_dtype, m, n, k, workspace,
+                  workspace_bytes, stream);
+}
+
+size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k) {
+  if (wfmt < W_BF16 || wfmt > W_FP4_G16E || m <= 0 || n <= 0 || k <= 0) return 0;
+  const int kc = 256 * vals_of(wfmt);
+  const int chunks = (k + kc - 1) / kc;
+  if (chunks < 2) return 0;
+  // Largest need over the tile choices the planner can make for this M.
+  size_t best = 0;
+  for (int mt = tile_for(m); mt >= 1; mt /= 2) {
+    const size_t need = workspace_need((m + mt - 1) / mt, mt, n, chunks);
+    if (need > best) best = need;
+  }
+  return best;
+}
+
+int klab_cbf16_unpack(const void* payload, const uint32_t* metadata, uint16_t* out, int n, int k, void* stream) {
+  if (!payload || !metadata || !out || n <= 0 || k <= 0) return KLAB_E_INVALID;
+  return launch_cbf16_unpack(payload, metadata, out, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int klab_int8_dequantize(const int8_t* codes, const float* scales, int group, float* out, int n, int k,
+                         void* stream) {
+  if (!codes || !scales || !out || n <= 0 || k <= 0) return KLAB_E_INVALID;
+  if (group != 0 && group != 64) return KLAB_E_UNSUPPORTED;
+  if (group == 64 && k % 64) return KLAB_E_SHAPE;
+  return launch_int8_dequant(codes, scales, group, out, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int klab_fp4_dequantize(const uint8_t* packed, const void* scales, int scale_kind, const float* gscale, float* out,
+                        int n, int k, void* stream) {
+  if (!packed || !scales || !out || n <= 0 || k <= 0) return KLAB_E_INVALID;
+  if (scale_kind == KLAB_FP4_E4M3_G16) {
+    if (!gscale) return KLAB_E_INVALID;
+    if (k % 16) return KLAB_E_SHAPE;
+  } else if (scale_kind == KLAB_FP4_F16_G32) {
+    if (k % 32) return KLAB_E_SHAPE;
+  } else {
+    return KLAB_E_UNSUPPORTED;
+  }
+  return launch_fp4_dequant(packed, scales, scale_kind, gscale, out, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int klab_l2_prefetch(const void* p, long long bytes, int blocks, int threads, int stride, int kind, unsigned* sink,
+                     void* stream) {
+  if (!p || bytes < 0 || blocks <= 0 || threads <= 0 || threads > 1024 || stride <= 0) return KLAB_E_INVALID;
+  if (kind != KLAB_L2_HINT && kind != KLAB_L2_HINT_LAST && kind != KLAB_L2_LOAD) return KLAB_E_UNSUPPORTED;
+  if (kind == KLAB_L2_LOAD && !sink) return KLAB_E_INVALID;
+  return launch_l2_prefetch(p, bytes, blocks, stride, threads, kind, sink, static_cast<cudaStream_t>(stream));
+}
+
+int klab_set_option(int option, int value) {
+  switch (option) {
+    case KLAB_OPT_PDL: g_opt_pdl.store(value ? 1 : 0); return 0;
+    case KLAB_OPT_SPLIT:
+      if (value < -1 || value > 1) return KLAB_E_INVALID;
+      g_opt_split.store(value);
+      return 0;
+    case KLAB_OPT_GENERIC: g_opt_generic.store(value ? 1 : 0); return 0;
+    default: return KLAB_E_INVALID;
+  }
+}
+
+int klab_get_option(int option) {
+  switch (option) {
+    case KLAB_OPT_PDL: return g_opt_pdl.load();
+    case KLAB_OPT_SPLIT: return g_opt_split.load();
+    case KLAB_OPT_GENERIC: return g_opt_generic.load();
+    default: return KLAB_E_INVALID;
+  }
+}
+
+int klab_device_status(int clear) {
+  DeviceInfo* info = nullptr;
+  int rc = current_device_info(&info);
+  if (rc) return rc;
+  int value = 0;
+  cudaError_t err = cudaMemcpy(&value, info->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return err;
+  if (clear && value) {
+    const int zero = 0;
+    err = cudaMemcpy(info->status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) return err;
+  }
+  return value;
+}
+
+const char* klab_error_string(int code) {
+  switch (code) {
+    case 0: return "success";
+    case KLAB_E_DRIVER: return "Cannot load CUDA driver or required symbols";
+    case KLAB_E_NO_CONTEXT: return "No current CUDA context; initialize PyTorch CUDA first";
+    case KLAB_E_INVALID: return "Invalid null argument or launch dimensions";
+    case KLAB_E_SHAPE: return "Shape not supported by this weight format";
+    case KLAB_E_ALIGN: return "Pointer or stride alignment not supported";
+    case KLAB_E_UNSUPPORTED: return "Unsupported dtype or format combination";
+    case KLAB_E_DEVICE: return "A kernel recorded a device-side error (bounded wait expired)";
+    default:
+      if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
+      return "Unknown klab error";
+  }
+}
+
+int klab_version(void) { return 1; }
+
+}  // extern "C"

@@ -1,0 +1,16 @@
+// Internal declarations shared by the CUDA translation units of libklab_b200.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "../../include/klab_b200.h"
+
+namespace klab {
+cudaError_t launch_cbf16_unpack(const void* payload, const unsigned* metadata, void* out, int n, int k,
+                                cudaStream_t stream);
+cudaError_t launch_int8_dequant(const void* codes, const float* scales, int group, float* out, int n, int k,
+                                cudaStream_t stream);
+cudaError_t launch_fp4_dequant(const void* packed, const void* scales, int kind, const float* gscale, float* out,
+                               int n, int k, cudaStream_t stream);
+cudaError_t launch_l2_prefetch(const void* p, long long bytes, int blocks, int stride, int threads, int kind,
+                               unsigned* sink, cudaStream_t stream);
+}  // namespace klab

@@ -1,0 +1,51 @@
+// L2 prefetch side-stream kernels, under the reference's names and argument ABI
+// (research/l2-prefetch/src/prefetch_kernels.cu:3-25):
+//   (const char* p, long long bytes, int stride, unsigned* sink)
+// Grid-stride over [p, p + bytes), one request per `stride` bytes; none of them
+// writes the range. Built into libklab_b200.so (klab_l2_prefetch) and, unchanged,
+// into a standalone cubin that the lab_* driver ABI loads by name.
+#include "common.cuh"
+#include "klab_kernels.h"
+
+extern "C" __global__ void l2_hint(const char* p, long long bytes, int stride, unsigned* sink) {
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x * stride;
+  for (long long off = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * stride; off < bytes;
+       off += step)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p + off));
+}
+
+// Lines marked evict_last.
+extern "C" __global__ void l2_hint_last(const char* p, long long bytes, int stride, unsigned* sink) {
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x * stride;
+  for (long long off = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * stride; off < bytes;
+       off += step)
+    asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(p + off));
+}
+
+// Real loads that bypass L1 (ld.global.cg). The xor keeps them live; the store is
+// guarded by an impossible condition (bytes < 0) and never executes.
+extern "C" __global__ void l2_load(const char* p, long long bytes, int stride, unsigned* sink) {
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x * stride;
+  unsigned acc = 0;
+  for (long long off = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * stride; off < bytes;
+       off += step) {
+    unsigned v;
+    asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p + off));
+    acc ^= v;
+  }
+  if (bytes < 0 && acc == 0x9e3779b9u) sink[0] = acc;
+}
+
+namespace klab {
+cudaError_t launch_l2_prefetch(const void* p, long long bytes, int blocks, int stride, int threads, int kind,
+                               unsigned* sink, cudaStream_t stream) {
+  const char* c = static_cast<const char*>(p);
+  if (kind == KLAB_L2_HINT)
+    l2_hint<<<blocks, threads, 0, stream>>>(c, bytes, stride, sink);
+  else if (kind == KLAB_L2_HINT_LAST)
+    l2_hint_last<<<blocks, threads, 0, stream>>>(c, bytes, stride, sink);
+  else
+    l2_load<<<blocks, threads, 0, stream>>>(c, bytes, stride, sink);
+  return cudaGetLastError();
+}
+}  // namespace klab
