@@ -15,10 +15,12 @@
  * rows (a column shard) gives bit-identical values to the full projection.
  *
  * Workspace: projections may split K across thread blocks when N is small.
- * That needs `workspace` of klab_gemv_workspace_bytes(...) bytes, zero-filled
- * once before first use and then left alone (every launch leaves it zeroed).
- * Pass NULL / 0 to disable splitting; results are identical either way. One
- * workspace must not be used by launches that can run concurrently.
+ * That needs `workspace` of klab_gemv_workspace_bytes(...) bytes (16-byte
+ * aligned), zero-filled once before first use and then left alone: its first
+ * 64 KiB hold completion tickets that every launch leaves zeroed, the rest is
+ * scratch for partial sums. Pass NULL / 0 to disable splitting; results are
+ * identical either way. One workspace must not be used by launches that can
+ * run concurrently.
  */
 #ifndef KLAB_B200_H
 #define KLAB_B200_H

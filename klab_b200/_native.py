@@ -9,11 +9,14 @@ runs the sm_100a kernels of this library.
 from __future__ import annotations
 
 import ctypes as ct
+import os
 import threading
 from pathlib import Path
 
 LIB_DIR = Path(__file__).resolve().parent / "_lib"
-LIB_PATH = LIB_DIR / "libklab_b200.so"
+# KLAB_B200_LIBRARY selects another build of the same library (e.g. one compiled
+# with different ring depth or warp count); the default is the in-tree build.
+LIB_PATH = Path(os.environ.get("KLAB_B200_LIBRARY", LIB_DIR / "libklab_b200.so"))
 PREFETCH_CUBIN = LIB_DIR / "prefetch_kernels.cubin"
 
 # include/klab_b200.h constants

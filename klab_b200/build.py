@@ -78,8 +78,15 @@ def _compile(source: Path, headers, verbose=False) -> Path:
     return obj
 
 
-def build(clean: bool = False, verbose: bool = False) -> Path:
-    """Compile every kernel for sm_100a and link libklab_b200.so; return its path."""
+def build(clean: bool = False, verbose: bool = False, out_dir: Path | None = None, defines=()) -> Path:
+    """Compile every kernel for sm_100a and link libklab_b200.so; return its path.
+    out_dir/defines build a variant (e.g. defines=("KLAB_DEPTH=4",)) elsewhere."""
+    global OUT, OBJ, LIBRARY, ALIAS, PREFETCH_CUBIN, EXPORTS, NVCC_FLAGS
+    if out_dir is not None:
+        OUT = Path(out_dir)
+        OBJ, LIBRARY, ALIAS = OUT / "obj", OUT / "libklab_b200.so", OUT / "libkernel_lab.so"
+        PREFETCH_CUBIN, EXPORTS = OUT / "prefetch_kernels.cubin", OUT / "exports.map"
+    NVCC_FLAGS = NVCC_FLAGS + [f"-D{d}" for d in defines]
     if clean and OUT.exists():
         shutil.rmtree(OUT)
     OBJ.mkdir(parents=True, exist_ok=True)

@@ -18,6 +18,10 @@ __device__ int g_status_word;
 namespace {
 
 constexpr size_t kXSmemCap = 96 * 1024;       // FP32 x staging budget per CTA
+// Split-K workspace layout: [tickets: kTicketCap u32][partials]. The ticket region
+// has a fixed size so that launches of different shapes sharing one workspace
+// never see another launch's partials where they expect zeroed tickets.
+constexpr size_t kTicketCap = 16384;
 constexpr size_t kMaxSmem = 227 * 1024;
 
 std::atomic<int> g_opt_pdl{1};
@@ -155,8 +159,7 @@ int shape_ok(int wfmt, int k) {
 }
 
 size_t workspace_need(int tiles, int mt, int n, int chunks) {
-  const size_t tickets = ((static_cast<size_t>(tiles) * n * 4 + 255) / 256) * 256;
-  return tickets + static_cast<size_t>(tiles) * mt * n * chunks * 4;
+  return kTicketCap * 4 + static_cast<size_t>(tiles) * mt * n * chunks * 4;
 }
 
 int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const void* aux, const float* gscale,
@@ -230,7 +233,8 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
   p.use_tma = (g_opt_generic.load() == 0) && tma_eligible(wfmt, w, aux, k);
 
   const size_t need = workspace_need(tiles, mt, n, chunks);
-  const bool can_split = ws && ws_bytes >= need && chunks >= 2 && aligned16(ws);
+  const bool can_split = ws && ws_bytes >= need && chunks >= 2 && aligned16(ws) &&
+                         static_cast<size_t>(tiles) * n <= kTicketCap;
   const int opt = g_opt_split.load();
   const bool split = can_split && (opt == 1 || (opt == -1 && chunks >= 3 &&
                                                 static_cast<long long>(n) * 2 < static_cast<long long>(gmax) * kWarps));
@@ -241,7 +245,7 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
     grid_x = static_cast<int>(want < gmax ? want : gmax);
     p.split = 1;
     p.tickets = static_cast<unsigned*>(ws);
-    p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + ((static_cast<size_t>(tiles) * n * 4 + 255) / 256) * 256);
+    p.ws = reinterpret_cast<float*>(static_cast<char*>(ws) + kTicketCap * 4);
   } else {
     grid_x = n < gmax ? n : gmax;
     p.split = 0;
@@ -315,7 +319,7 @@ size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k) {
   if (wfmt < W_BF16 || wfmt > W_FP4_G16E || m <= 0 || n <= 0 || k <= 0) return 0;
   const int kc = 256 * vals_of(wfmt);
   const int chunks = (k + kc - 1) / kc;
-  if (chunks < 2) return 0;
+  if (chunks < 2 || static_cast<size_t>(n) > kTicketCap) return 0;
   // Largest need over the tile choices the planner can make for this M.
   size_t best = 0;
   for (int mt = tile_for(m); mt >= 1; mt /= 2) {

@@ -53,8 +53,18 @@ enum XFmt : int { X_BF16 = 0, X_F16 = 1, X_F32 = 2 };
 // Where x lives while the tile is computed.
 enum XMode : int { XM_SMEM = 0, XM_GLOBAL = 1 };
 
-constexpr int kWarps = 8;             // warps per CTA
-constexpr int kDepth = 3;             // ring slots per warp
+#ifndef KLAB_WARPS
+#define KLAB_WARPS 8
+#endif
+#ifndef KLAB_DEPTH
+#define KLAB_DEPTH 3
+#endif
+#ifndef KLAB_SEG_UNROLL
+#define KLAB_SEG_UNROLL 1
+#endif
+constexpr int kWarps = KLAB_WARPS;    // warps per CTA
+constexpr int kDepth = KLAB_DEPTH;    // ring slots per warp
+constexpr int kSegUnroll = KLAB_SEG_UNROLL;
 constexpr int kSegs = 8;              // segments per chunk
 constexpr int kWeightSlot = 4096;     // weight bytes per full chunk
 constexpr int kMetaRing = 2 * kDepth - 1;  // coded: metadata entries per warp
@@ -328,7 +338,7 @@ __device__ __forceinline__ void compute_item(const GemvParams& p, const float* x
     chain[t] = f2{0.0f, 0.0f};
     acc[t] = 0.0f;
   }
-#pragma unroll 1
+#pragma unroll(kSegUnroll)
   for (int j = 0; j < kSegs; ++j) {
     const int lcol = (32 * j + lane) * VALS;  // chunk-relative column of v = 0
     if (32 * VALS * j >= L) break;

@@ -126,12 +126,13 @@ def quantize_weights(w):
 
 
 def quantize_weights_f16(w):
-    """BASELINE format: per 32 values an FP16 scale = max|g|/6 (RNE to FP16),
+    """BASELINE format: per 32 values an FP16 scale = max|g|/6 (IEEE division, RNE to FP16),
     nearest-even E2M1 codes against that scale."""
     _check_source(w, 32)
     n, k = w.shape
     blocks = w.reshape(n, k // 32, 32)
-    scales = (blocks.abs().amax(-1) / 6.0).to(torch.float16)
+    amax = blocks.abs().amax(-1)
+    scales = (amax / amax.new_tensor(6.0)).to(torch.float16)  # IEEE division
     tiny = torch.finfo(torch.float32).tiny
     codes = _e2m1_codes(blocks / scales.float().clamp_min(tiny).unsqueeze(-1)).reshape(n, k)
     return FP4F16Weights(_pack(codes), scales.contiguous())

@@ -50,10 +50,13 @@ class Int8Weights:
         return int8_linear(x, self.codes, self.scales, threads)
 
 
-def _quantize_groups(blocks):
+def _quantize_groups(blocks, ieee_division=False):
+    """ieee_division=False divides by the Python number 127 as the reference does
+    (on CUDA: a multiply by fl32(1/127)); True divides by a device tensor (IEEE)."""
     amax = blocks.abs().amax(-1)
     tiny = torch.finfo(torch.float32).tiny
-    scale = torch.where(amax > 0, (amax / 127).clamp_min(tiny), torch.ones_like(amax))
+    divisor = amax.new_tensor(127.0) if ieee_division else 127
+    scale = torch.where(amax > 0, (amax / divisor).clamp_min(tiny), torch.ones_like(amax))
     codes = torch.round(blocks / scale.unsqueeze(-1)).clamp_(-127, 127).to(torch.int8)
     return codes, scale
 
@@ -77,10 +80,11 @@ def quantize_weights(w):
 
 
 def quantize_weights_per_row(w):
-    """Per-row scale = max|row|/127, same rounding rules."""
+    """Per-row scale = max|row|/127 with an IEEE division,
+    otherwise the reference's rounding rules."""
     _check_source(w, 1)
     n, k = w.shape
-    codes, scale = _quantize_groups(w.reshape(n, 1, k))
+    codes, scale = _quantize_groups(w.reshape(n, 1, k), ieee_division=True)
     return Int8Weights(codes.reshape(n, k).contiguous(), scale.reshape(n).contiguous())
 
 

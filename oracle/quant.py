@@ -3,16 +3,23 @@
 Test infrastructure only (see oracle/__init__.py). All arithmetic is IEEE FP32
 with round-to-nearest-even, exactly as the reference's torch code computes it:
 
+* Scalar divisors: the reference's quantizers run only on CUDA tensors, where
+  torch divides a tensor by a Python number as a multiply by the FP32
+  reciprocal (a * fl(1/b)); on CPU it is a true IEEE division. The two differ
+  by one ulp in a few percent of groups. semantics="cuda" (default) reproduces
+  the reference's device results; semantics="cpu" reproduces the same code run
+  on CPU (how tests/golden/make_golden.py produced its fixtures).
 * INT8, reference format (int8_weights.py:15-35): per 64-value group,
   scale = max|w|/127 (clamped to FP32 tiny; 1.0 for an all-zero group),
   code = clamp(round_half_even(w / scale), -127, 127); dequant = code * scale.
-* INT8, per-row: the same with one group per row.
+* INT8, per-row: one group per row, true IEEE division.
 * FP4, reference format (fp4.py:21-60): global = max|W|/(448*6) (tiny-clamped,
   1.0 when W == 0); per 16 values an E4M3 scale = RNE_e4m3(min(max|g| / (6*global), 448));
   E2M1 codes by nearest value with ties to even (the bucketize + tie fix of
   fp4.py:53-58), sign bit from signbit(w / scale); low nibble = even k;
   dequant = e2m1 * (e4m3 * global).
-* FP4, FP16 scale per 32 (BASELINE config 3): scale = RNE_fp16(max|g| / 6);
+* FP4, FP16 scale per 32: scale = RNE_fp16(max|g| / 6)
+  with a true IEEE division;
   codes as above against that scale; dequant = e2m1 * scale (exact in FP32).
 """
 
@@ -31,9 +38,20 @@ _E2M1_BOUNDS = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], dtype=np.float3
 
 # ------------------------------------------------------------------ INT8
 
-def _int8_quantize_groups(groups: np.ndarray):
+def scalar_divide(a, b: float, semantics: str) -> np.ndarray:
+    """a / b for an FP32 array a and a Python number b, as torch computes it on
+    `semantics` = "cuda" (a * fl32(1/b)) or "cpu" (IEEE division)."""
+    a = np.asarray(a, dtype=F32)
+    if semantics == "cuda":
+        return (a * (F32(1) / F32(b))).astype(F32)
+    if semantics == "cpu":
+        return (a / F32(b)).astype(F32)
+    raise ValueError("semantics must be 'cuda' or 'cpu'")
+
+
+def _int8_quantize_groups(groups: np.ndarray, semantics: str):
     amax = np.abs(groups).max(axis=-1)
-    scale = np.where(amax > 0, np.maximum(amax / F32(127), TINY), F32(1)).astype(F32)
+    scale = np.where(amax > 0, np.maximum(scalar_divide(amax, 127, semantics), TINY), F32(1)).astype(F32)
     codes = np.clip(np.rint(groups / scale[..., None]), -127, 127).astype(np.int8)
     return codes, scale
 
@@ -49,17 +67,17 @@ def _check_weights(w, multiple):
     return n, k
 
 
-def int8_quantize_g64(w: np.ndarray):
+def int8_quantize_g64(w: np.ndarray, semantics: str = "cuda"):
     """Reference INT8 format (int8_weights.py:23-35): codes int8 [N,K], scales fp32 [N,K/64]."""
     n, k = _check_weights(w, 64)
-    codes, scales = _int8_quantize_groups(w.reshape(n, k // 64, 64))
+    codes, scales = _int8_quantize_groups(w.reshape(n, k // 64, 64), semantics)
     return codes.reshape(n, k), scales
 
 
 def int8_quantize_row(w: np.ndarray):
     """Per-row INT8: codes int8 [N,K], scales fp32 [N]."""
     n, k = _check_weights(w, 1)
-    codes, scales = _int8_quantize_groups(w.reshape(n, 1, k))
+    codes, scales = _int8_quantize_groups(w.reshape(n, 1, k), "cpu")
     return codes.reshape(n, k), scales.reshape(n)
 
 
@@ -135,13 +153,13 @@ def unpack_nibbles(packed: np.ndarray) -> np.ndarray:
 
 # ------------------------------------------------------------------ FP4 formats
 
-def fp4_quantize_e4m3(w: np.ndarray):
+def fp4_quantize_e4m3(w: np.ndarray, semantics: str = "cuda"):
     """Reference FP4 format (fp4.py:33-60): packed uint8 [N,K/2], E4M3 scale bytes
     [N,K/16], global scale fp32 (shape ())."""
     n, k = _check_weights(w, 16)
     blocks = w.reshape(n, k // 16, 16)
     amax = np.abs(w).max()
-    glob = F32(max(amax / F32(448.0 * 6.0), TINY)) if amax > 0 else F32(1)
+    glob = F32(max(scalar_divide(amax, 448.0 * 6.0, semantics), TINY)) if amax > 0 else F32(1)
     block_scale = np.minimum(np.abs(blocks).max(axis=-1) / (F32(6.0) * glob), F32(448)).astype(F32)
     scales = f32_to_e4m3(block_scale)
     decoded = (e4m3_to_f32(scales) * glob).astype(F32)

@@ -120,7 +120,7 @@ def test_check_outputs_known_answers():
 
 
 def test_int8_quantizer_matches_reference(quant):
-    codes, scales = oq.int8_quantize_g64(quant["w"])
+    codes, scales = oq.int8_quantize_g64(quant["w"], semantics="cpu")
     np.testing.assert_array_equal(codes, quant["int8__codes"])
     np.testing.assert_array_equal(scales.view(np.uint32), quant["int8__scales"].view(np.uint32))
     deq = oq.int8_dequantize(codes, scales)
@@ -131,7 +131,7 @@ def test_int8_quantizer_matches_reference(quant):
 @pytest.mark.parametrize("case", ["fp4", "ties"])
 def test_fp4_quantizer_matches_reference(quant, case):
     w = quant["w"] if case == "fp4" else quant["ties"]
-    packed, scales, glob = oq.fp4_quantize_e4m3(w)
+    packed, scales, glob = oq.fp4_quantize_e4m3(w, semantics="cpu")
     np.testing.assert_array_equal(packed, quant[f"{case}__packed"])
     np.testing.assert_array_equal(scales, quant[f"{case}__scales"])
     assert np.float32(glob).view(np.uint32) == np.float32(quant[f"{case}__global"]).view(np.uint32)
@@ -141,7 +141,7 @@ def test_fp4_quantizer_matches_reference(quant, case):
 
 
 def test_fp4_zero_tensor(quant):
-    packed, scales, glob = oq.fp4_quantize_e4m3(np.zeros((5, 16), dtype=np.float32))
+    packed, scales, glob = oq.fp4_quantize_e4m3(np.zeros((5, 16), dtype=np.float32), semantics="cpu")
     np.testing.assert_array_equal(packed, quant["zero__fp4_packed"])
     assert float(glob) == float(quant["zero__fp4_global"]) == 1.0
     assert not oq.fp4_dequantize_e4m3(packed, scales, glob).any()
@@ -179,3 +179,16 @@ def test_baseline_variants_round_trip():
     assert packed.shape == (16, 64) and s16.dtype == np.float16
     deq = oq.fp4_dequantize_f16(packed, s16)
     assert np.abs(deq - w).max() <= np.abs(w).max() / 6 * 1.01
+
+
+def test_cuda_scalar_division_semantics():
+    """torch on CUDA divides by a Python number as a multiply by the FP32
+    reciprocal; the oracle's "cuda" semantics differ from "cpu" by one ulp at most."""
+    a = np.float32(np.random.default_rng(0).random(10000) * 3).astype(np.float32)
+    cuda, cpu = oq.scalar_divide(a, 127, "cuda"), oq.scalar_divide(a, 127, "cpu")
+    diff = np.abs(cuda.view(np.int32).astype(np.int64) - cpu.view(np.int32).astype(np.int64))
+    assert diff.max() == 1 and 0 < np.count_nonzero(diff) < 0.2 * a.size
+    w = np.random.default_rng(1).standard_normal((64, 256)).astype(np.float32)
+    c1, s1 = oq.int8_quantize_g64(w, "cuda")
+    c2, s2 = oq.int8_quantize_g64(w, "cpu")
+    assert np.abs(s1.view(np.int32).astype(np.int64) - s2.view(np.int32)).max() <= 1
