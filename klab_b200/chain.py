@@ -75,11 +75,18 @@ class ProjectionChain:
     process group (NCCL) when world > 1."""
 
     def __init__(self, shape: ChainShape = ChainShape(), *, rank=0, world=1, device=None, group=None,
-                 seed=0, std=0.02, weights=None):
+                 seed=0, std=0.02, weights=None, project=None):
+        """weights(layer, name, rows) -> BF16 tensor supplies shard weights (default:
+        seeded N(0, std^2)); project(x, w, n_rows, k, out, ldo) replaces the native
+        projection (host-side tests drive the sharding and gathers on CPU with it)."""
         self.shape = shape
         self.rank, self.world, self.group = rank, world, group
-        self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
-        get_module(self.device)
+        if project is None:
+            self.device = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+            get_module(self.device)
+        else:
+            self.device = torch.device("cpu") if device is None else torch.device(device)
+        self._project = project
         stage_a, (dname, dn, dk) = shape.projections()
         m = shape.tokens
         self.layers = []
@@ -102,7 +109,7 @@ class ProjectionChain:
         self.a_out = {name: torch.zeros((m, n), **bf) for name, n in stage_a if name not in ("up",)}
         self.up_full = torch.zeros((m, shape.ffn), **bf)       # gather buffer for up
         self.graph = None
-        self.stream = torch.cuda.Stream(self.device)
+        self.stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
 
     def weight_bytes(self):
         return sum(w.numel() * 2 for layer in self.layers for (w, _, _) in layer.values())
@@ -111,9 +118,13 @@ class ProjectionChain:
         return 7 * self.shape.layers
 
     def _proj(self, x, w, rows, n, out, k):
+        """Rows [r0, r1) of this projection into columns [r0, r1) of the full-width `out`."""
         m = x.shape[0]
-        rc_out = out[:, rows[0]:] if out.shape[1] == n else out
-        _native.gemv(_native.W_BF16, _native.DT_BF16, x, w, None, None, rc_out, _native.DT_BF16, m,
+        dst = out[:, rows[0]:]
+        if self._project is not None:
+            self._project(x, w, rows[1] - rows[0], k, dst, out.shape[1])
+            return
+        _native.gemv(_native.W_BF16, _native.DT_BF16, x, w, None, None, dst, _native.DT_BF16, m,
                      rows[1] - rows[0], k, ldo=out.shape[1])
 
     def _gather(self, full, n):

@@ -17,7 +17,10 @@ __device__ int g_status_word;
 
 namespace {
 
-constexpr size_t kXSmemCap = 96 * 1024;       // FP32 x staging budget per CTA
+constexpr size_t kXSmemCap = 96 * 1024;       // x staging budget per CTA
+#ifndef KLAB_PREFER_X16
+#define KLAB_PREFER_X16 KLAB_MIXED_BF16      // stage 16-bit x unconverted for 16-bit weights
+#endif
 // Split-K workspace layout: [tickets: kTicketCap u32][partials]. The ticket region
 // has a fixed size so that launches of different shapes sharing one workspace
 // never see another launch's partials where they expect zeroed tickets.
@@ -189,8 +192,13 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
 
   int mt = tile_for(m);
   int xmode = XM_SMEM;
+  const bool x16 = KLAB_PREFER_X16 && (wfmt == W_BF16 || wfmt == W_F16 || wfmt == W_CBF16) && xdt != KLAB_DT_F32;
   for (;;) {
-    if (static_cast<size_t>(mt) * kpad * 4 <= kXSmemCap) {
+    if (x16 && static_cast<size_t>(mt) * kpad * 2 <= kXSmemCap) {
+      xmode = XM_SMEM16;
+      break;
+    }
+    if (!x16 && static_cast<size_t>(mt) * kpad * 4 <= kXSmemCap) {
       xmode = XM_SMEM;
       break;
     }
@@ -210,7 +218,8 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
   s.mt = mt;
   s.pdl = g_opt_pdl.load() != 0;
   s.smem = bar_region_bytes(wfmt) + kWarps * warp_region_bytes(wfmt) +
-           (xmode == XM_SMEM ? static_cast<size_t>(mt) * kpad * 4 : 0);
+           (xmode == XM_SMEM ? static_cast<size_t>(mt) * kpad * 4
+                             : xmode == XM_SMEM16 ? static_cast<size_t>(mt) * kpad * 2 : 0);
   if (s.smem > kMaxSmem) return KLAB_E_SHAPE;
   const int occ = occupancy(wfmt, s);
   if (occ <= 0) return KLAB_E_UNSUPPORTED;

@@ -73,8 +73,12 @@ cudaError_t run_mt(const GemvParams& p, const LaunchShape& s, cudaStream_t strea
 // (weight format, x format) pair.
 template <int F, int X>
 cudaError_t run_fx(const GemvParams& p, const LaunchShape& s, cudaStream_t stream, int* occ) {
-  return s.xmode == XM_SMEM ? run_mt<F, X, XM_SMEM>(p, s, stream, occ)
-                            : run_mt<F, X, XM_GLOBAL>(p, s, stream, occ);
+  if (s.xmode == XM_SMEM) return run_mt<F, X, XM_SMEM>(p, s, stream, occ);
+  if (s.xmode == XM_GLOBAL) return run_mt<F, X, XM_GLOBAL>(p, s, stream, occ);
+  // 16-bit x staging exists for the 16-bit-weight formats only.
+  if constexpr (X != X_F32 && (F == W_BF16 || F == W_F16 || F == W_CBF16))
+    return run_mt<F, X, XM_SMEM16>(p, s, stream, occ);
+  return cudaErrorNotSupported;
 }
 
 // Defined in gemv_<family>.cu; dispatch on (wfmt, s.xfmt). Unsupported pairs

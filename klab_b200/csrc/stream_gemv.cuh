@@ -22,10 +22,12 @@
 //   * chunk c covers columns [c*KC, min(K, (c+1)*KC)), KC = 256*VALS;
 //   * segment j (0..7) of a chunk, lane l: values v = 0..VALS-1 at column
 //     c*KC + 32*VALS*j + VALS*l + v;
-//   * unscaled formats: per lane two FP32 chains (even v, odd v), fma.rn, run over
-//     the chunk's segments in order; lane partial = even + odd;
-//   * scaled formats: per lane and scale group the same two chains start at zero,
-//     g = even + odd, then acc = fma.rn(g, scale, acc) in segment order;
+//   * unscaled formats: per lane eight FP32 sums s0..s7, value v feeding s[v % 8]
+//     with fma.rn, running over the chunk's segments in order; lane partial =
+//     ((s0+s1)+(s2+s3))+((s4+s5)+(s6+s7));
+//   * scaled formats: per lane and scale group the same eight sums start at
+//     zero, g = their tree, then acc = fma.rn(g, scale, acc) in segment order;
+//     lane partial = acc;
 //   * chunk partial = butterfly warp sum of lane partials;
 //   * row total = ((P0 + P1) + P2) + ... over chunks in order;
 //   * per-row scale (W_I8_ROW) or global scale (W_FP4_G16E): one fp32 multiply;
@@ -51,7 +53,7 @@ enum WFmt : int {
 };
 enum XFmt : int { X_BF16 = 0, X_F16 = 1, X_F32 = 2 };
 // Where x lives while the tile is computed.
-enum XMode : int { XM_SMEM = 0, XM_GLOBAL = 1 };
+enum XMode : int { XM_SMEM = 0, XM_GLOBAL = 1, XM_SMEM16 = 2 };
 
 #ifndef KLAB_WARPS
 #define KLAB_WARPS 8
@@ -134,17 +136,13 @@ struct GemvParams {
 
 // ------------------------------------------------------------------ x staging
 
-// x in shared memory is FP32 in a lane-interleaved layout: for token t, segment
-// g (global, 32*VALS columns) and 16-byte vector i of a lane's VALS values, lane
-// l's vector sits at ((t*G + g)*NV + i)*32 + l (16-byte units). A warp's
-// ld.shared.v4 of vector i of one segment therefore touches 512 consecutive
-// bytes: no bank conflicts. Columns >= K are zero.
-template <int F>
-struct XLayout {
-  static constexpr int VALS = WTraits<F>::VALS;
-  static constexpr int NV = VALS / 4;  // fp32 vectors per lane per segment
-};
-
+// x lives in shared memory in a lane-interleaved layout. For token t, global
+// segment g (32*VALS columns) and 16-byte vector i of a lane's VALS values,
+// lane l's vector is 16-byte unit ((t*G + g)*NV + i)*32 + l. A warp's
+// ld.shared.v4 of vector i of one segment touches 512 consecutive bytes: no
+// bank conflicts. XM_SMEM stores FP32 (NV = VALS/4); XM_SMEM16 stores the
+// 16-bit input values unchanged (NV = VALS/8, BF16/FP16 x only). Columns >= K
+// and tokens >= M are zero.
 template <int X>
 __device__ __forceinline__ float x_value(const void* x, long long idx) {
   if constexpr (X == X_BF16) {
@@ -156,74 +154,89 @@ __device__ __forceinline__ float x_value(const void* x, long long idx) {
   }
 }
 
-template <int F, int X, int MT>
-__device__ void stage_x(const GemvParams& p, int tile, float* xs, int kpad) {
+template <int F, int XM>
+struct XLayout {
+  static constexpr int VALS = WTraits<F>::VALS;
+  static constexpr int EB = (XM == XM_SMEM16) ? 2 : 4;  // bytes per staged value
+  static constexpr int NV = VALS * EB / 16;             // 16-byte vectors per lane per segment
+  static constexpr int SEG_BYTES = NV * 512;            // one segment of one token
+};
+
+template <int F, int X, int XM, int MT>
+__device__ void stage_x(const GemvParams& p, int tile, unsigned char* xs, int segs) {
   constexpr int VALS = WTraits<F>::VALS;
-  constexpr int NV = VALS / 4;
-  const int segs = kpad / (32 * VALS);
-  const int total = MT * kpad;
-  for (int e = threadIdx.x; e < total; e += blockDim.x) {
-    const int t = e / kpad;
-    const int col = e - t * kpad;
+  constexpr int EB = XLayout<F, XM>::EB;
+  constexpr int PER = 16 / EB;  // values per 16-byte unit
+  constexpr int NV = XLayout<F, XM>::NV;
+  const int kpad = segs * 32 * VALS;
+  const int units = MT * kpad / PER;
+  for (int u = threadIdx.x; u < units; u += blockDim.x) {
+    const int t = u / (kpad / PER);
+    const int col0 = (u - t * (kpad / PER)) * PER;  // first column of this unit
     const int token = tile * MT + t;
-    float v = 0.0f;
-    if (token < p.m && col < p.k) v = x_value<X>(p.x, static_cast<long long>(token) * p.ldx + col);
-    const int g = col / (32 * VALS);
-    const int r = col - g * 32 * VALS;
+    const int g = col0 / (32 * VALS);
+    const int r = col0 - g * 32 * VALS;
     const int l = r / VALS;
-    const int vv = r - l * VALS;
-    const int i = vv >> 2;
-    xs[((((t * segs + g) * NV + i) * 32 + l) << 2) + (vv & 3)] = v;
+    const int i = (r - l * VALS) / PER;
+    unsigned char* dst = xs + ((((t * segs + g) * NV + i) * 32 + l) << 4);
+    if constexpr (EB == 4) {
+      float v[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = col0 + e;
+        v[e] = (token < p.m && col < p.k) ? x_value<X>(p.x, static_cast<long long>(token) * p.ldx + col) : 0.0f;
+      }
+      *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+      unsigned short v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const int col = col0 + e;
+        v[e] = (token < p.m && col < p.k)
+                   ? static_cast<const unsigned short*>(p.x)[static_cast<long long>(token) * p.ldx + col]
+                   : static_cast<unsigned short>(0);
+      }
+      *reinterpret_cast<uint4*>(dst) =
+          make_uint4(v[0] | (unsigned(v[1]) << 16), v[2] | (unsigned(v[3]) << 16), v[4] | (unsigned(v[5]) << 16),
+                     v[6] | (unsigned(v[7]) << 16));
+    }
   }
 }
 
-// The lane's VALS activation values (FP32) of token t at global segment g.
+// The lane's VALS activations of one token and segment, widened to FP32.
+// XM_SMEM / XM_SMEM16: `addr` is the shared address of the lane's first vector;
+// XM_GLOBAL: `src` points at the lane's first value in global memory (16-byte
+// aligned, K % VALS == 0 guaranteed by the host).
 template <int F, int X, int XM>
-__device__ __forceinline__ void load_x(const GemvParams& p, const float* xs, int segs, int t,
-                                       int token, int g, int lane, int col,
-                                       float (&xv)[WTraits<F>::VALS]) {
+__device__ __forceinline__ void load_x(unsigned addr, const void* src, float (&xv)[WTraits<F>::VALS]) {
   constexpr int VALS = WTraits<F>::VALS;
-  constexpr int NV = VALS / 4;
   if constexpr (XM == XM_SMEM) {
-    const unsigned base = smem_addr(xs) + static_cast<unsigned>((((t * segs + g) * NV) * 32 + lane) * 16);
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      uint4 v = lds128(base + i * 512);
+    for (int i = 0; i < VALS / 4; ++i) {
+      uint4 v = lds128(addr + i * 512);
       xv[4 * i + 0] = __uint_as_float(v.x);
       xv[4 * i + 1] = __uint_as_float(v.y);
       xv[4 * i + 2] = __uint_as_float(v.z);
       xv[4 * i + 3] = __uint_as_float(v.w);
     }
   } else {
-    // Global (L1-cached) reads; the host guarantees 16-byte alignment and
-    // K % VALS == 0 for this mode.
-    const char* row = static_cast<const char*>(p.x);
-    if constexpr (X == X_F32) {
-      const float* src = reinterpret_cast<const float*>(row) + static_cast<long long>(token) * p.ldx + col;
+    constexpr int XB = (X == X_F32) ? 4 : 2;
 #pragma unroll
-      for (int i = 0; i < VALS / 4; ++i) {
-        uint4 v = ldg128_cached(src + 4 * i);
-        xv[4 * i + 0] = __uint_as_float(v.x);
-        xv[4 * i + 1] = __uint_as_float(v.y);
-        xv[4 * i + 2] = __uint_as_float(v.z);
-        xv[4 * i + 3] = __uint_as_float(v.w);
-      }
-    } else {
-      const unsigned short* src =
-          reinterpret_cast<const unsigned short*>(row) + static_cast<long long>(token) * p.ldx + col;
+    for (int i = 0; i < VALS * XB / 16; ++i) {
+      uint4 v;
+      if constexpr (XM == XM_SMEM16)
+        v = lds128(addr + i * 512);
+      else
+        v = ldg128_cached(static_cast<const char*>(src) + 16 * i);
+      const unsigned q[4] = {v.x, v.y, v.z, v.w};
+      if constexpr (X == X_F32) {
 #pragma unroll
-      for (int i = 0; i < VALS / 8; ++i) {
-        uint4 v = ldg128_cached(src + 8 * i);
-        unsigned wv[4] = {v.x, v.y, v.z, v.w};
+        for (int e = 0; e < 4; ++e) xv[4 * i + e] = __uint_as_float(q[e]);
+      } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          if constexpr (X == X_BF16) {
-            xv[8 * i + 2 * q] = bf16lo(wv[q]);
-            xv[8 * i + 2 * q + 1] = bf16hi(wv[q]);
-          } else {
-            xv[8 * i + 2 * q] = f16lo(wv[q]);
-            xv[8 * i + 2 * q + 1] = f16hi(wv[q]);
-          }
+        for (int e = 0; e < 4; ++e) {
+          xv[8 * i + 2 * e] = (X == X_BF16) ? bf16lo(q[e]) : f16lo(q[e]);
+          xv[8 * i + 2 * e + 1] = (X == X_BF16) ? bf16hi(q[e]) : f16hi(q[e]);
         }
       }
     }
@@ -240,6 +253,7 @@ __device__ __forceinline__ float cbf16_code(unsigned code, unsigned base) {
 }
 
 // Weights of lane `lane`, segment j of the item in `slot` (shared address).
+// Fixed-size formats read the lane's 16 bytes at slot + (32*j + lane)*16.
 template <int F>
 __device__ __forceinline__ void load_w(unsigned slot, unsigned meta_entry, unsigned first_unit,
                                        int j, int lane, float (&w)[WTraits<F>::VALS]) {
@@ -322,27 +336,100 @@ __device__ __forceinline__ void load_w(unsigned slot, unsigned meta_entry, unsig
 
 // ------------------------------------------------------------------ item math
 
-// Chunk partial for each token of the tile (identical in every lane).
-template <int F, int X, int XM, int MT>
-__device__ __forceinline__ void compute_item(const GemvParams& p, const float* xs, int segs,
-                                             int tile, int c, int L, unsigned slot,
-                                             unsigned meta_entry, unsigned first_unit, int lane,
-                                             float (&P)[MT]) {
+#ifndef KLAB_MIXED_BF16
+#define KLAB_MIXED_BF16 0
+#endif
+
+// acc = x * w + acc with BF16 (or FP16) x and w taken from the low or high half
+// of a 32-bit word: the product is exact in FP32 and the sum is rounded once,
+// exactly like widening both to FP32 and using fma.rn.f32.
+template <bool HI, bool F16>
+__device__ __forceinline__ float fma_half_mixed(unsigned x2, unsigned w2, float acc) {
+  float d;
+  if constexpr (F16) {
+    if constexpr (HI)
+      asm("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
+          " fma.rn.f32.f16 %0, xh, wh, %3;\n}\n" : "=f"(d) : "r"(x2), "r"(w2), "f"(acc));
+    else
+      asm("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
+          " fma.rn.f32.f16 %0, xl, wl, %3;\n}\n" : "=f"(d) : "r"(x2), "r"(w2), "f"(acc));
+  } else {
+    if constexpr (HI)
+      asm("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
+          " fma.rn.f32.bf16 %0, xh, wh, %3;\n}\n" : "=f"(d) : "r"(x2), "r"(w2), "f"(acc));
+    else
+      asm("{\n .reg .b16 xl, xh, wl, wh;\n mov.b32 {xl, xh}, %1;\n mov.b32 {wl, wh}, %2;\n"
+          " fma.rn.f32.bf16 %0, xl, wl, %3;\n}\n" : "=f"(d) : "r"(x2), "r"(w2), "f"(acc));
+  }
+  return d;
+}
+
+// True when a (weight format, x mode) pair multiplies 16-bit operands directly.
+template <int F, int XM>
+struct MixedPath {
+  static constexpr bool value = KLAB_MIXED_BF16 && (F == W_BF16 || F == W_F16) && XM == XM_SMEM16;
+};
+
+// Lane accumulators of one token: eight FP32 sums held as four pairs. Value v
+// of a lane's vector goes to sum (v % 8): pair (v / 2) % 4, half v % 2.
+struct Acc8 {
+  f2 a[4];
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = f2{0.0f, 0.0f};
+  }
+  // ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7))
+  __device__ __forceinline__ float tree() const {
+    return add_rn(add_rn(add_rn(a[0].x, a[0].y), add_rn(a[1].x, a[1].y)),
+                  add_rn(add_rn(a[2].x, a[2].y), add_rn(a[3].x, a[3].y)));
+  }
+};
+
+// Chunk partial of every token of the tile (the same value in every lane).
+// FULL: the chunk has all KC columns (no bounds checks). xs_lane: shared address
+// of token 0's first x vector for this lane and chunk (XM_SMEM*); xg: pointer to
+// token 0's first value for this lane and chunk (XM_GLOBAL).
+template <int F, int X, int XM, int MT, bool FULL>
+__device__ __forceinline__ void compute_item(unsigned slot, unsigned meta_entry, unsigned first_unit, int lane,
+                                             int L, unsigned xs_lane, int tok_stride, const char* xg,
+                                             long long xg_stride, int tvalid, float (&P)[MT]) {
   constexpr int VALS = WTraits<F>::VALS;
-  constexpr int KC = Layout<F>::KC;
   constexpr bool SCALED = (F == W_I8_G64 || F == W_FP4_G32H || F == W_FP4_G16E);
-  f2 chain[MT];
+  constexpr bool MIXED = MixedPath<F, XM>::value;
+  constexpr int SEG = XLayout<F, XM>::SEG_BYTES;
+  constexpr int XB = (X == X_F32) ? 4 : 2;
+  Acc8 acc8[MT];
   float acc[MT];
 #pragma unroll
   for (int t = 0; t < MT; ++t) {
-    chain[t] = f2{0.0f, 0.0f};
+    acc8[t].zero();
     acc[t] = 0.0f;
   }
-#pragma unroll(kSegUnroll)
+  // Full unrolling of the segment loop pays for one or two tokens; wider tiles
+  // would exceed the register budget.
+  constexpr int UNROLL = MT <= 2 ? kSegUnroll : (kSegUnroll < 2 ? kSegUnroll : 2);
+#pragma unroll(UNROLL)
   for (int j = 0; j < kSegs; ++j) {
-    const int lcol = (32 * j + lane) * VALS;  // chunk-relative column of v = 0
-    if (32 * VALS * j >= L) break;
-    if (lcol < L) {
+    if (!FULL) {
+      if (32 * VALS * j >= L) break;
+      if ((32 * j + lane) * VALS >= L) continue;
+    }
+    const unsigned xs_seg = xs_lane + j * SEG;
+    const char* xg_seg = xg + static_cast<long long>(32 * VALS * j) * XB;
+    if constexpr (MIXED) {
+      const uint4 wv = lds128(slot + (j * 32 + lane) * 16);
+      const unsigned wq[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        const uint4 xv = lds128(xs_seg + t * tok_stride);
+        const unsigned xq[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc8[t].a[i].x = fma_half_mixed<false, F == W_F16>(xq[i], wq[i], acc8[t].a[i].x);
+          acc8[t].a[i].y = fma_half_mixed<true, F == W_F16>(xq[i], wq[i], acc8[t].a[i].y);
+        }
+      }
+    } else {
       float w[VALS];
       load_w<F>(slot, meta_entry, first_unit, j, lane, w);
       float s0 = 1.0f, s1 = 1.0f;
@@ -355,39 +442,37 @@ __device__ __forceinline__ void compute_item(const GemvParams& p, const float* x
         s0 = f16lo(h);
         s1 = f16hi(h);
       }
-      const int g = (c * KC + 32 * VALS * j) / (32 * VALS);
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
-        // Tokens past M (ragged last tile) read row M-1; their sums are never stored.
-        const int token = min(tile * MT + t, p.m - 1);
         float xv[VALS];
-        load_x<F, X, XM>(p, xs, segs, t, token, g, lane, c * KC + lcol, xv);
+        // Global mode: tokens past M (ragged last tile) re-read the last valid
+        // token; their sums are never stored.
+        load_x<F, X, XM>(xs_seg + t * tok_stride, xg_seg + min(t, tvalid - 1) * xg_stride, xv);
         if constexpr (!SCALED) {
 #pragma unroll
-          for (int v = 0; v < VALS; v += 2)
-            chain[t] = fma2(f2{xv[v], xv[v + 1]}, f2{w[v], w[v + 1]}, chain[t]);
-        } else if constexpr (F == W_FP4_G16E) {
-          f2 ga{0.0f, 0.0f}, gb{0.0f, 0.0f};
-#pragma unroll
-          for (int v = 0; v < 16; v += 2) ga = fma2(f2{xv[v], xv[v + 1]}, f2{w[v], w[v + 1]}, ga);
-#pragma unroll
-          for (int v = 16; v < 32; v += 2) gb = fma2(f2{xv[v], xv[v + 1]}, f2{w[v], w[v + 1]}, gb);
-          acc[t] = fma_rn(add_rn(ga.x, ga.y), s0, acc[t]);
-          acc[t] = fma_rn(add_rn(gb.x, gb.y), s1, acc[t]);
+          for (int v = 0; v < VALS; v += 2) {
+            f2& a = acc8[t].a[(v >> 1) & 3];
+            a = fma2(f2{xv[v], xv[v + 1]}, f2{w[v], w[v + 1]}, a);
+          }
         } else {
-          f2 ga{0.0f, 0.0f};
+          constexpr int GROUP = (F == W_FP4_G16E) ? 16 : VALS;
 #pragma unroll
-          for (int v = 0; v < VALS; v += 2) ga = fma2(f2{xv[v], xv[v + 1]}, f2{w[v], w[v + 1]}, ga);
-          acc[t] = fma_rn(add_rn(ga.x, ga.y), s0, acc[t]);
+          for (int g0 = 0; g0 < VALS; g0 += GROUP) {
+            Acc8 sub;
+            sub.zero();
+#pragma unroll
+            for (int v = g0; v < g0 + GROUP; v += 2) {
+              f2& a = sub.a[(v >> 1) & 3];
+              a = fma2(f2{xv[v], xv[v + 1]}, f2{w[v], w[v + 1]}, a);
+            }
+            acc[t] = fma_rn(sub.tree(), g0 == 0 ? s0 : s1, acc[t]);
+          }
         }
       }
     }
   }
 #pragma unroll
-  for (int t = 0; t < MT; ++t) {
-    const float lane_partial = SCALED ? acc[t] : add_rn(chain[t].x, chain[t].y);
-    P[t] = warp_allsum(lane_partial);
-  }
+  for (int t = 0; t < MT; ++t) P[t] = warp_allsum(SCALED ? acc[t] : acc8[t].tree());
 }
 
 // ------------------------------------------------------------------ filling
@@ -434,6 +519,17 @@ __device__ __forceinline__ void warp_copy_bytes(char* dst, const char* src, int 
 
 // ------------------------------------------------------------------ kernel
 
+// (row, chunk) position in a warp's item sequence.
+struct Cursor {
+  int row, c;
+  __device__ __forceinline__ void advance(int chunks, int row_step) {
+    if (++c == chunks) {
+      c = 0;
+      row += row_step;
+    }
+  }
+};
+
 template <int F, int MT>
 __device__ __forceinline__ void finalize_token(const GemvParams& p, int row, int token, float v,
                                                float row_scale) {
@@ -456,6 +552,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
   constexpr int VALS = WTraits<F>::VALS;
   constexpr bool CODED = (F == W_CBF16);
   constexpr int BAR_REGION = ((kWarps * Layout<F>::BARS * 8 + 127) / 128) * 128;
+  constexpr int XB = (X == X_F32) ? 4 : 2;
   extern __shared__ __align__(128) unsigned char smem[];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -467,74 +564,62 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
   const unsigned slot0 = smem_addr(smem) + BAR_REGION + warp * Layout<F>::WARP_BYTES;
   const unsigned meta0 = slot0 + kDepth * SLOT;
   unsigned char* slot0_ptr = smem + BAR_REGION + warp * Layout<F>::WARP_BYTES;
-  float* xs = reinterpret_cast<float*>(smem + BAR_REGION + kWarps * Layout<F>::WARP_BYTES);
-  const int kpad = ((k + 32 * VALS - 1) / (32 * VALS)) * (32 * VALS);
-  const int segs = kpad / (32 * VALS);
+  unsigned char* xs = smem + BAR_REGION + kWarps * Layout<F>::WARP_BYTES;
+  const int segs = (k + 32 * VALS - 1) / (32 * VALS);
 
-  // This warp's items: (row, chunk) pairs in processing order.
-  int r0 = 0, nitems = 0;
+  // This warp's items, as (row, chunk) cursors that advance without division:
+  // aligned mode deals whole rows round-robin (row step kWarps); split mode gives
+  // each warp a contiguous run of items (row step 1).
+  int nitems = 0, row_step = kWarps;
+  Cursor start{0, 0};
   long long wbegin = 0, wend = 0;
   if (!p.split) {
-    const int g = gridDim.x;
-    const int b = blockIdx.x;
-    r0 = static_cast<int>(static_cast<long long>(n) * b / g);
-    const int r1 = static_cast<int>(static_cast<long long>(n) * (b + 1) / g);
+    const int r0 = static_cast<int>(static_cast<long long>(n) * blockIdx.x / gridDim.x);
+    const int r1 = static_cast<int>(static_cast<long long>(n) * (blockIdx.x + 1) / gridDim.x);
     const int rows = r1 - r0 - warp > 0 ? (r1 - r0 - warp + kWarps - 1) / kWarps : 0;
     nitems = rows * S;
+    start = Cursor{r0 + warp, 0};
   } else {
     const long long T = static_cast<long long>(n) * S;
     const long long i0 = T * blockIdx.x / gridDim.x, i1 = T * (blockIdx.x + 1) / gridDim.x;
     wbegin = i0 + (i1 - i0) * warp / kWarps;
     wend = i0 + (i1 - i0) * (warp + 1) / kWarps;
     nitems = static_cast<int>(wend - wbegin);
+    start = Cursor{static_cast<int>(wbegin / S), static_cast<int>(wbegin % S)};
+    row_step = 1;
   }
-  auto item_rc = [&](int q, int& row, int& c) {
-    if (!p.split) {
-      row = r0 + warp + kWarps * (q / S);
-      c = q - (q / S) * S;
-    } else {
-      const long long gi = wbegin + q;
-      row = static_cast<int>(gi / S);
-      c = static_cast<int>(gi - static_cast<long long>(row) * S);
-    }
-  };
+  Cursor cur = start, iss = start, mcur = start;
 
-  // lane 0: bulk copy of item q's metadata (coded) into its ring entry.
-  auto issue_meta = [&](int q) {
-    int row, c;
-    item_rc(q, row, c);
-    const int nb = min(32, k / 64 - 32 * c);
-    const unsigned bar = mbar0 + (q % kMetaRing) * 8;
-    const char* src = static_cast<const char*>(p.aux) + (static_cast<long long>(row) * (k / 64) + 32 * c) * 4;
+  // lane 0: bulk copy of the metadata of item `ix` (coded) at cursor m.
+  auto issue_meta = [&](int ix, const Cursor& m) {
+    const int nb = min(32, k / 64 - 32 * m.c);
+    const unsigned bar = mbar0 + (ix % kMetaRing) * 8;
+    const char* src = static_cast<const char*>(p.aux) + (static_cast<long long>(m.row) * (k / 64) + 32 * m.c) * 4;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(bar, nb * 4);
-    bulk_g2s(meta0 + (q % kMetaRing) * kMetaEntry, src, nb * 4, bar);
+    bulk_g2s(meta0 + (ix % kMetaRing) * kMetaEntry, src, nb * 4, bar);
   };
-  // lane 0: bulk copy of item q's weight bytes (+ scales) into slot q % kDepth.
-  auto issue_item = [&](int q) {
-    int row, c;
-    item_rc(q, row, c);
-    const int L = min(KC, k - c * KC);
-    const unsigned slot = slot0 + (q % kDepth) * SLOT;
-    const unsigned bar = pbar0 + (q % kDepth) * 8;
+  // lane 0: bulk copy of item `ix`'s weight bytes (+ scales) at cursor it.
+  auto issue_item = [&](int ix, const Cursor& it) {
+    const int L = min(KC, k - it.c * KC);
+    const unsigned slot = slot0 + (ix % kDepth) * SLOT;
+    const unsigned bar = pbar0 + (ix % kDepth) * 8;
     const char* src;
     int bytes;
-    const char* ssrc;
-    int sbytes;
+    const char* ssrc = nullptr;
+    int sbytes = 0;
     if constexpr (CODED) {
-      const unsigned entry = meta0 + (q % kMetaRing) * kMetaEntry;
+      const unsigned entry = meta0 + (ix % kMetaRing) * kMetaEntry;
       const int nb = L / 64;
       const unsigned m0 = lds32(entry), ml = lds32(entry + 4 * (nb - 1));
       const unsigned off = (m0 & 0x7fffffu) << 5;
       const unsigned end = ((ml & 0x7fffffu) << 5) + ((ml >> 31) ? 128u : 96u);
       src = static_cast<const char*>(p.w) + off;
       bytes = static_cast<int>(end - off);
-      ssrc = nullptr;
-      sbytes = 0;
     } else {
-      src = static_cast<const char*>(p.w) + w_offset_bytes<F>(static_cast<long long>(row) * k + c * KC);
+      src = static_cast<const char*>(p.w) + w_offset_bytes<F>(static_cast<long long>(it.row) * k + it.c * KC);
       bytes = static_cast<int>(w_offset_bytes<F>(L));
-      scale_span<F>(p, row, c, L, &ssrc, &sbytes);
+      scale_span<F>(p, it.row, it.c, L, &ssrc, &sbytes);
     }
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(bar, bytes + sbytes);
@@ -543,7 +628,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
   };
 
   bool ok = true;
-  int issued_meta = 0, issued = 0;  // lane 0 bookkeeping (items issued so far)
+  int issued_meta = 0, issued = 0;  // lane 0 bookkeeping
   if (p.use_tma) {
     if (lane == 0) {
       for (int i = 0; i < Layout<F>::BARS; ++i) mbar_init(pbar0 + 8 * i, 1);
@@ -554,36 +639,51 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
     // in flight before griddepcontrol.wait.
     if (lane == 0) {
       if constexpr (CODED) {
-        for (; issued_meta < min(kMetaRing, nitems); ++issued_meta) issue_meta(issued_meta);
+        for (; issued_meta < min(kMetaRing, nitems); ++issued_meta) {
+          issue_meta(issued_meta, mcur);
+          mcur.advance(S, row_step);
+        }
         for (; issued < min(kDepth - 1, nitems); ++issued) {
           if (!mbar_wait(mbar0 + (issued % kMetaRing) * 8, (issued / kMetaRing) & 1)) {
             ok = false;
             break;
           }
-          issue_item(issued);
+          issue_item(issued, iss);
+          iss.advance(S, row_step);
         }
       } else {
-        for (; issued < min(kDepth - 1, nitems); ++issued) issue_item(issued);
+        for (; issued < min(kDepth - 1, nitems); ++issued) {
+          issue_item(issued, iss);
+          iss.advance(S, row_step);
+        }
       }
     }
     ok = __shfl_sync(0xffffffffu, ok, 0);
   }
 
   grid_dependency_wait();
-  if constexpr (XM == XM_SMEM) stage_x<F, X, MT>(p, tile, xs, kpad);
+  if constexpr (XM != XM_GLOBAL) stage_x<F, X, XM, MT>(p, tile, xs, segs);
   __syncthreads();
   grid_launch_dependents();
+
+  constexpr int SEG = XLayout<F, XM>::SEG_BYTES;
+  const int tok_stride = segs * SEG;
+  const unsigned xs_lane0 = smem_addr(xs) + lane * 16;
+  const char* xg_lane0 =
+      static_cast<const char*>(p.x) + (static_cast<long long>(tile * MT) * p.ldx + lane * VALS) * XB;
+  const long long xg_stride = static_cast<long long>(p.ldx) * XB;
+  const int tvalid = min(MT, p.m - tile * MT);
 
   float rowsum[MT];
 #pragma unroll
   for (int t = 0; t < MT; ++t) rowsum[t] = 0.0f;
   float row_scale = 1.0f;
+  bool row_complete = true;
   int contributed = 0;
 
   int q = 0;
   for (; q < nitems && ok; ++q) {
-    int row, c;
-    item_rc(q, row, c);
+    const int row = cur.row, c = cur.c;
     const int L = min(KC, k - c * KC);
     const unsigned slot = slot0 + (q % kDepth) * SLOT;
     const unsigned entry = meta0 + (q % kMetaRing) * kMetaEntry;
@@ -592,7 +692,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
         bool ready = true;
         if constexpr (CODED) ready = mbar_wait(mbar0 + (issued % kMetaRing) * 8, (issued / kMetaRing) & 1);
         if (ready) {
-          issue_item(issued);
+          issue_item(issued, iss);
+          iss.advance(S, row_step);
           ++issued;
         } else {
           ok = false;
@@ -611,7 +712,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
       if constexpr (CODED) {
         unsigned* ep = reinterpret_cast<unsigned*>(slot0_ptr + kDepth * SLOT + (q % kMetaRing) * kMetaEntry);
         const int nb = L / 64;
-        if (lane < nb) ep[lane] = __ldg(static_cast<const unsigned*>(p.aux) + static_cast<long long>(row) * (k / 64) + 32 * c + lane);
+        if (lane < nb)
+          ep[lane] = __ldg(static_cast<const unsigned*>(p.aux) + static_cast<long long>(row) * (k / 64) + 32 * c + lane);
         __syncwarp();
         const unsigned m0 = ep[0], ml = ep[nb - 1];
         const unsigned off = (m0 & 0x7fffffu) << 5;
@@ -626,24 +728,31 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
           const char* ssrc;
           int sbytes;
           scale_span<F>(p, row, c, L, &ssrc, &sbytes);
-          warp_copy_bytes(reinterpret_cast<char*>(sp) + kWeightSlot, ssrc, sbytes,
-                          WTraits<F>::SCALE_BYTES, lane);
+          warp_copy_bytes(reinterpret_cast<char*>(sp) + kWeightSlot, ssrc, sbytes, WTraits<F>::SCALE_BYTES,
+                          lane);
         }
       }
       __syncwarp();
     }
 
-    if constexpr (F == W_I8_ROW) {
-      if (c == 0 || q == 0) row_scale = __ldg(static_cast<const float*>(p.aux) + row);
+    if (c == 0 || q == 0) {
+      if constexpr (F == W_I8_ROW) row_scale = __ldg(static_cast<const float*>(p.aux) + row);
+      if (p.split)
+        row_complete = static_cast<long long>(row) * S >= wbegin && static_cast<long long>(row) * S + S <= wend;
     }
     const unsigned first_unit = CODED ? (lds32(entry) & 0x7fffffu) : 0u;
+    const unsigned xs_lane = xs_lane0 + c * kSegs * SEG;
+    const char* xg = xg_lane0 + static_cast<long long>(c) * KC * XB;
     float P[MT];
-    compute_item<F, X, XM, MT>(p, xs, segs, tile, c, L, slot, entry, first_unit, lane, P);
+    if (L == KC)
+      compute_item<F, X, XM, MT, true>(slot, entry, first_unit, lane, L, xs_lane, tok_stride, xg, xg_stride, tvalid,
+                                       P);
+    else
+      compute_item<F, X, XM, MT, false>(slot, entry, first_unit, lane, L, xs_lane, tok_stride, xg, xg_stride,
+                                        tvalid, P);
     __syncwarp();  // every lane is done with this slot before it is refilled
 
-    const bool complete = !p.split || (static_cast<long long>(row) * S >= wbegin &&
-                                       static_cast<long long>(row) * S + S <= wend);
-    if (complete) {
+    if (row_complete) {
 #pragma unroll
       for (int t = 0; t < MT; ++t) rowsum[t] = (c == 0) ? P[t] : add_rn(rowsum[t], P[t]);
       if (c == S - 1) {
@@ -673,7 +782,6 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
         contributed = 0;
         if (last) {
           __threadfence();
-          if constexpr (F == W_I8_ROW) row_scale = __ldg(static_cast<const float*>(p.aux) + row);
 #pragma unroll
           for (int t = 0; t < MT; ++t) {
             const int token = tile * MT + t;
@@ -688,10 +796,12 @@ __global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvP
         }
       }
     }
+    cur.advance(S, row_step);
 
     if constexpr (CODED) {
       if (p.use_tma && lane == 0 && issued_meta < nitems && issued_meta == q + kMetaRing) {
-        issue_meta(issued_meta);
+        issue_meta(issued_meta, mcur);
+        mcur.advance(S, row_step);
         ++issued_meta;
       }
     }
