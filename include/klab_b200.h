@@ -77,6 +77,7 @@ extern "C" {
 #define KLAB_OPT_PDL 0        /* 1 (default): launch with programmatic dependent launch */
 #define KLAB_OPT_SPLIT 1      /* -1 (default) automatic, 0 never, 1 always (when workspace allows) */
 #define KLAB_OPT_GENERIC 2    /* 1: force the cooperative-load (non bulk-copy) fill path */
+#define KLAB_OPT_CTAS_PER_SM 3 /* cap on projection CTAs per SM (0, default: as many as fit) */
 
 /* ---------------------------------------------------------------- projections */
 

@@ -30,6 +30,7 @@ constexpr size_t kMaxSmem = 227 * 1024;
 std::atomic<int> g_opt_pdl{1};
 std::atomic<int> g_opt_split{-1};
 std::atomic<int> g_opt_generic{0};
+std::atomic<int> g_opt_ctas_per_sm{0};  // 0: as many as fit
 
 struct DeviceInfo {
   bool ready = false;
@@ -89,9 +90,9 @@ size_t warp_region_bytes(int wfmt) {
   }
 }
 
-size_t bar_region_bytes(int wfmt) {
+size_t bar_region_bytes(int wfmt, int warps) {
   const int bars = kDepth + (wfmt == W_CBF16 ? kMetaRing : 0);
-  return ((static_cast<size_t>(kWarps) * bars * 8 + 127) / 128) * 128;
+  return ((static_cast<size_t>(warps) * bars * 8 + 127) / 128) * 128;
 }
 
 int tile_for(int m) { return m == 1 ? 1 : m == 2 ? 2 : m <= 4 ? 4 : 8; }
@@ -217,12 +218,15 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
   s.xmode = xmode;
   s.mt = mt;
   s.pdl = g_opt_pdl.load() != 0;
-  s.smem = bar_region_bytes(wfmt) + kWarps * warp_region_bytes(wfmt) +
+  const int warps = warps_for(mt);
+  s.smem = bar_region_bytes(wfmt, warps) + warps * warp_region_bytes(wfmt) +
            (xmode == XM_SMEM ? static_cast<size_t>(mt) * kpad * 4
                              : xmode == XM_SMEM16 ? static_cast<size_t>(mt) * kpad * 2 : 0);
   if (s.smem > kMaxSmem) return KLAB_E_SHAPE;
-  const int occ = occupancy(wfmt, s);
+  int occ = occupancy(wfmt, s);
   if (occ <= 0) return KLAB_E_UNSUPPORTED;
+  const int cap = g_opt_ctas_per_sm.load();
+  if (cap > 0 && cap < occ) occ = cap;
   const int gmax = occ * info->sms / tiles > 0 ? occ * info->sms / tiles : 1;
 
   GemvParams p = {};
@@ -246,11 +250,11 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
                          static_cast<size_t>(tiles) * n <= kTicketCap;
   const int opt = g_opt_split.load();
   const bool split = can_split && (opt == 1 || (opt == -1 && chunks >= 3 &&
-                                                static_cast<long long>(n) * 2 < static_cast<long long>(gmax) * kWarps));
+                                                static_cast<long long>(n) * 2 < static_cast<long long>(gmax) * warps));
   int grid_x;
   if (split) {
     const long long items = static_cast<long long>(n) * chunks;
-    const long long want = (items + kWarps - 1) / kWarps;
+    const long long want = (items + warps - 1) / warps;
     grid_x = static_cast<int>(want < gmax ? want : gmax);
     p.split = 1;
     p.tickets = static_cast<unsigned*>(ws);
@@ -381,6 +385,10 @@ int klab_set_option(int option, int value) {
       g_opt_split.store(value);
       return 0;
     case KLAB_OPT_GENERIC: g_opt_generic.store(value ? 1 : 0); return 0;
+    case KLAB_OPT_CTAS_PER_SM:
+      if (value < 0 || value > 32) return KLAB_E_INVALID;
+      g_opt_ctas_per_sm.store(value);
+      return 0;
     default: return KLAB_E_INVALID;
   }
 }
@@ -390,6 +398,7 @@ int klab_get_option(int option) {
     case KLAB_OPT_PDL: return g_opt_pdl.load();
     case KLAB_OPT_SPLIT: return g_opt_split.load();
     case KLAB_OPT_GENERIC: return g_opt_generic.load();
+    case KLAB_OPT_CTAS_PER_SM: return g_opt_ctas_per_sm.load();
     default: return KLAB_E_INVALID;
   }
 }

@@ -117,6 +117,17 @@ __device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
   return d;
 }
 
+// d = a + b on both halves, each rounded once to nearest even (add.rn.f32x2).
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  unsigned long long ra, rb, rd;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(ra) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(rb) : "f"(b.x), "f"(b.y));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+  f2 d;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d.x), "=f"(d.y) : "l"(rd));
+  return d;
+}
+
 __device__ __forceinline__ float fma_rn(float a, float b, float c) {
   float d;
   asm("fma.rn.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));

@@ -56,15 +56,19 @@ enum XFmt : int { X_BF16 = 0, X_F16 = 1, X_F32 = 2 };
 enum XMode : int { XM_SMEM = 0, XM_GLOBAL = 1, XM_SMEM16 = 2 };
 
 #ifndef KLAB_WARPS
-#define KLAB_WARPS 8
+#define KLAB_WARPS 16      // warps per CTA for single-token tiles
+#endif
+#ifndef KLAB_WARPS_MT
+#define KLAB_WARPS_MT 8    // warps per CTA for multi-token tiles (register budget)
 #endif
 #ifndef KLAB_DEPTH
-#define KLAB_DEPTH 3
+#define KLAB_DEPTH 2
 #endif
 #ifndef KLAB_SEG_UNROLL
-#define KLAB_SEG_UNROLL 1
+#define KLAB_SEG_UNROLL 8
 #endif
-constexpr int kWarps = KLAB_WARPS;    // warps per CTA
+// Warps per CTA for a token tile of MT.
+__host__ __device__ constexpr int warps_for(int mt) { return mt == 1 ? KLAB_WARPS : KLAB_WARPS_MT; }
 constexpr int kDepth = KLAB_DEPTH;    // ring slots per warp
 constexpr int kSegUnroll = KLAB_SEG_UNROLL;
 constexpr int kSegs = 8;              // segments per chunk
@@ -313,9 +317,12 @@ __device__ __forceinline__ void load_w(unsigned slot, unsigned meta_entry, unsig
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
 #pragma unroll
-      for (int b = 0; b < 4; ++b) {
-        const float f = __uint_as_float(__byte_perm(q[i], 0x4b000000u, 0x7540u + b));
-        w[4 * i + b] = add_rn(f, -8388736.0f);
+      for (int b = 0; b < 4; b += 2) {
+        const f2 u{__uint_as_float(__byte_perm(q[i], 0x4b000000u, 0x7540u + b)),
+                   __uint_as_float(__byte_perm(q[i], 0x4b000000u, 0x7541u + b))};
+        const f2 v = add2(u, f2{-8388736.0f, -8388736.0f});
+        w[4 * i + b] = v.x;
+        w[4 * i + b + 1] = v.y;
       }
     }
   } else {
@@ -337,7 +344,7 @@ __device__ __forceinline__ void load_w(unsigned slot, unsigned meta_entry, unsig
 // ------------------------------------------------------------------ item math
 
 #ifndef KLAB_MIXED_BF16
-#define KLAB_MIXED_BF16 0
+#define KLAB_MIXED_BF16 1
 #endif
 
 // acc = x * w + acc with BF16 (or FP16) x and w taken from the low or high half
@@ -543,10 +550,11 @@ __device__ __forceinline__ void finalize_token(const GemvParams& p, int row, int
   }
 }
 
-// Grid (G, ceil(M / MT)); block kWarps*32. Dynamic shared memory:
+// Grid (G, ceil(M / MT)); block warps_for(MT)*32. Dynamic shared memory:
 // [mbarriers][kWarps warp regions: kDepth slots (+ metadata ring)][x staging].
 template <int F, int X, int XM, int MT>
-__global__ void __launch_bounds__(kWarps * 32, 1) stream_gemv_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(const GemvParams p) {
+  constexpr int kWarps = warps_for(MT);
   constexpr int KC = Layout<F>::KC;
   constexpr int SLOT = Layout<F>::SLOT;
   constexpr int VALS = WTraits<F>::VALS;
