@@ -91,6 +91,16 @@ KLAB_API int klab_gemv(int wfmt, int xdtype, const void* x, int ldx, const void*
               const float* gscale, void* out, int ldo, int out_dtype, int m, int n, int k,
               void* workspace, size_t workspace_bytes, void* stream);
 
+/* Several projections that read the same x[M,K] in one launch: segment i has
+ * n[i] output rows, weights w[i] (+ aux[i]) and writes out[i][t * ldo[i] + row].
+ * 1 <= nseg <= 8. Every output equals the separate klab_gemv call bit for bit.
+ * Fuses what the reference launches one projection at a time, e.g. the QKV /
+ * gate-up groups of examples/kv_pair_projection.py:13-36. */
+KLAB_API int klab_gemv_multi(int wfmt, int xdtype, const void* x, int ldx, int nseg, const void* const* w,
+                             const void* const* aux, const float* gscale, void* const* out, const int* ldo,
+                             const int* n, int out_dtype, int m, int k, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
 /* BF16 x, raw BF16 W, BF16 or FP32 out.
  * Replaces compressed_bf16.raw_linear (compressed_bf16.py:450-460, kernels
  * cbf16_raw_{bf16,fp32}_t*_v*, compressed_kernels.cu:156-176) and
@@ -134,7 +144,8 @@ KLAB_API int klab_fp4_linear(const void* x, int xdtype, const uint8_t* packed, c
                     int scale_kind, const float* gscale, void* out, int out_dtype, int m, int n, int k,
                     void* workspace, size_t workspace_bytes, void* stream);
 
-/* Workspace bytes a klab_gemv call of this shape can use for split-K (0 = none). */
+/* Workspace bytes a klab_gemv call of this shape can use for split-K (0 = none);
+ * for klab_gemv_multi pass the total row count as n. */
 KLAB_API size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k);
 
 /* ---------------------------------------------------------------- decode */

@@ -33,6 +33,7 @@ _I = ct.c_int
 _SZ = ct.c_size_t
 _SIGNATURES = {
     "klab_gemv": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_gemv_multi": (_I, [_I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "klab_raw_linear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     "klab_coded_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     "klab_half_linear": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _SZ, _P]),
@@ -191,3 +192,26 @@ def gemv(wfmt, xdt, x, w, aux, gscale, out, out_dt, m, n, k, *, ldx=None, ldo=No
     check(rc, "klab_gemv")
     record(stream, x, w, aux, gscale, out)
     return out
+
+
+def gemv_multi(wfmt, xdt, x, segments, gscale, out_dt, m, k, *, ldx=None, workspace=True):
+    """One launch over several projections sharing x: segments is a list of
+    (w, aux, out_view, ldo, n_rows); out_view points at the first output element."""
+    import torch
+
+    nseg = len(segments)
+    device = x.device
+    stream = torch.cuda.current_stream(device)
+    total = sum(seg[4] for seg in segments)
+    ws_ptr, ws_bytes = (workspace_for(wfmt, m, total, k, device.index, stream) if workspace else (None, 0))
+    wp = (ct.c_void_p * nseg)(*[seg[0].data_ptr() for seg in segments])
+    ap = (ct.c_void_p * nseg)(*[(seg[1].data_ptr() if seg[1] is not None else None) for seg in segments])
+    op = (ct.c_void_p * nseg)(*[seg[2].data_ptr() for seg in segments])
+    ldo = (ct.c_int * nseg)(*[seg[3] for seg in segments])
+    ns = (ct.c_int * nseg)(*[seg[4] for seg in segments])
+    with torch.cuda.device(device):
+        rc = lib().klab_gemv_multi(wfmt, xdt, x.data_ptr(), k if ldx is None else ldx, nseg, wp, ap,
+                                   None if gscale is None else gscale.data_ptr(), op, ldo, ns, out_dt, m, k,
+                                   ws_ptr, ws_bytes, stream.cuda_stream)
+    check(rc, "klab_gemv_multi")
+    record(stream, x, *[t for seg in segments for t in (seg[0], seg[1], seg[2])])

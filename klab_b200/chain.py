@@ -75,7 +75,7 @@ class ProjectionChain:
     process group (NCCL) when world > 1."""
 
     def __init__(self, shape: ChainShape = ChainShape(), *, rank=0, world=1, device=None, group=None,
-                 seed=0, std=0.02, weights=None, project=None):
+                 seed=0, std=0.02, weights=None, project=None, fuse=True):
         """weights(layer, name, rows) -> BF16 tensor supplies shard weights (default:
         seeded N(0, std^2)); project(x, w, n_rows, k, out, ldo) replaces the native
         projection (host-side tests drive the sharding and gathers on CPU with it)."""
@@ -87,6 +87,9 @@ class ProjectionChain:
         else:
             self.device = torch.device("cpu") if device is None else torch.device(device)
         self._project = project
+        # One launch for the six stage-A projections (they share h and K); the
+        # outputs equal separate launches bit for bit.
+        self.fuse = fuse and project is None
         stage_a, (dname, dn, dk) = shape.projections()
         m = shape.tokens
         self.layers = []
@@ -115,7 +118,7 @@ class ProjectionChain:
         return sum(w.numel() * 2 for layer in self.layers for (w, _, _) in layer.values())
 
     def launches_per_step(self):
-        return 7 * self.shape.layers
+        return (2 if self.fuse else 7) * self.shape.layers
 
     def _proj(self, x, w, rows, n, out, k):
         """Rows [r0, r1) of this projection into columns [r0, r1) of the full-width `out`."""
@@ -150,12 +153,19 @@ class ProjectionChain:
         self.hbuf[0].copy_(x)
         for i, entry in enumerate(self.layers):
             h, nxt = self.hbuf[i % 2], self.hbuf[(i + 1) % 2]
-            for name, n in (("q", shape.hidden), ("k", shape.kv), ("v", shape.kv), ("o", shape.hidden),
-                            ("gate", shape.ffn)):
-                w, rows, _ = entry[name]
-                self._proj(h, w, rows, n, self.a_out[name], shape.hidden)
-            w, rows, _ = entry["up"]
-            self._proj(h, w, rows, shape.ffn, self.up_full, shape.hidden)
+            outs = dict(self.a_out, up=self.up_full)
+            if self.fuse:
+                segments = []
+                for name in ("q", "k", "v", "o", "gate", "up"):
+                    w, rows, n = entry[name]
+                    out = outs[name]
+                    segments.append((w, None, out[:, rows[0]:], out.shape[1], rows[1] - rows[0]))
+                _native.gemv_multi(_native.W_BF16, _native.DT_BF16, h, segments, None, _native.DT_BF16,
+                                   h.shape[0], shape.hidden)
+            else:
+                for name in ("q", "k", "v", "o", "gate", "up"):
+                    w, rows, n = entry[name]
+                    self._proj(h, w, rows, n, outs[name], shape.hidden)
             self._gather(self.up_full, shape.ffn)
             w, rows, _ = entry["down"]
             self._proj(self.up_full, w, rows, shape.hidden, nxt, shape.ffn)

@@ -166,17 +166,25 @@ size_t workspace_need(int tiles, int mt, int n, int chunks) {
   return kTicketCap * 4 + static_cast<size_t>(tiles) * mt * n * chunks * 4;
 }
 
-int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const void* aux, const float* gscale,
-             void* out, int ldo, int out_dt, int m, int n, int k, void* ws, size_t ws_bytes, void* stream) {
-  if (!x || !w || !out) return KLAB_E_INVALID;
-  if (m <= 0 || n <= 0 || k <= 0 || ldx < k || ldo < n) return KLAB_E_INVALID;
+int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const void* const* w,
+                   const void* const* aux, const float* gscale, void* const* out, const int* ldo, const int* nrows,
+                   int out_dt, int m, int k, void* ws, size_t ws_bytes, void* stream) {
+  if (!x || !w || !out || !ldo || !nrows || nseg < 1 || nseg > kMaxSegs) return KLAB_E_INVALID;
+  if (m <= 0 || k <= 0 || ldx < k) return KLAB_E_INVALID;
   if (wfmt < W_BF16 || wfmt > W_FP4_G16E) return KLAB_E_UNSUPPORTED;
   if (!x_compatible(wfmt, xdt)) return KLAB_E_UNSUPPORTED;
   if (out_dt != KLAB_DT_BF16 && out_dt != KLAB_DT_F32) return KLAB_E_UNSUPPORTED;
   const bool needs_aux = wfmt >= W_CBF16;
-  if (needs_aux && !aux) return KLAB_E_INVALID;
   if (wfmt == W_FP4_G16E && !gscale) return KLAB_E_INVALID;
   if (!shape_ok(wfmt, k)) return KLAB_E_SHAPE;
+  long long total = 0;
+  for (int i = 0; i < nseg; ++i) {
+    if (!w[i] || !out[i] || nrows[i] <= 0 || ldo[i] < nrows[i]) return KLAB_E_INVALID;
+    if (needs_aux && (!aux || !aux[i])) return KLAB_E_INVALID;
+    total += nrows[i];
+  }
+  if (total >= (1ll << 31)) return KLAB_E_SHAPE;
+  const int n = static_cast<int>(total);
 
   DeviceInfo* info = nullptr;
   int rc = current_device_info(&info);
@@ -231,19 +239,27 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
 
   GemvParams p = {};
   p.x = x;
-  p.w = w;
-  p.aux = aux;
   p.gscale = gscale;
-  p.out = out;
+  p.nseg = nseg;
+  bool tma = g_opt_generic.load() == 0;
+  int row0 = 0;
+  for (int i = 0; i < nseg; ++i) {
+    p.seg[i].w = w[i];
+    p.seg[i].aux = needs_aux ? aux[i] : nullptr;
+    p.seg[i].out = out[i];
+    p.seg[i].ldo = ldo[i];
+    p.seg[i].row0 = row0;
+    row0 += nrows[i];
+    tma = tma && tma_eligible(wfmt, w[i], needs_aux ? aux[i] : nullptr, k);
+  }
   p.status = info->status;
   p.m = m;
   p.n = n;
   p.k = k;
   p.ldx = ldx;
-  p.ldo = ldo;
   p.out_f32 = out_dt == KLAB_DT_F32;
   p.chunks = chunks;
-  p.use_tma = (g_opt_generic.load() == 0) && tma_eligible(wfmt, w, aux, k);
+  p.use_tma = tma;
 
   const size_t need = workspace_need(tiles, mt, n, chunks);
   const bool can_split = ws && ws_bytes >= need && chunks >= 2 && aligned16(ws) &&
@@ -265,6 +281,19 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
   }
   s.grid = dim3(grid_x, tiles, 1);
   return run_family(wfmt, p, s, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const void* aux, const float* gscale,
+             void* out, int ldo, int out_dt, int m, int n, int k, void* ws, size_t ws_bytes, void* stream) {
+  if (!x || !w || !out) return KLAB_E_INVALID;
+  if (m <= 0 || n <= 0 || k <= 0 || ldx < k || ldo < n) return KLAB_E_INVALID;
+  if (wfmt >= W_CBF16 && wfmt <= W_FP4_G16E && !aux) return KLAB_E_INVALID;
+  const void* ws_[1] = {w};
+  const void* as_[1] = {aux};
+  void* os_[1] = {out};
+  const int ldo_[1] = {ldo};
+  const int n_[1] = {n};
+  return run_gemv_multi(wfmt, xdt, x, ldx, 1, ws_, as_, gscale, os_, ldo_, n_, out_dt, m, k, ws, ws_bytes, stream);
 }
 
 }  // namespace
@@ -326,6 +355,13 @@ int klab_fp4_linear(const void* x, int xdtype, const uint8_t* packed, const void
     return KLAB_E_UNSUPPORTED;
   return run_gemv(wfmt, xdtype, x, k, packed, scales, gscale, out, n, out_dtype, m, n, k, workspace,
                   workspace_bytes, stream);
+}
+
+int klab_gemv_multi(int wfmt, int xdtype, const void* x, int ldx, int nseg, const void* const* w,
+                    const void* const* aux, const float* gscale, void* const* out, const int* ldo, const int* n,
+                    int out_dtype, int m, int k, void* workspace, size_t workspace_bytes, void* stream) {
+  return run_gemv_multi(wfmt, xdtype, x, ldx, nseg, w, aux, gscale, out, ldo, n, out_dtype, m, k, workspace,
+                        workspace_bytes, stream);
 }
 
 size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k) {

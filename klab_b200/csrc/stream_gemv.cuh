@@ -121,22 +121,50 @@ struct Layout {
   static constexpr int BARS = kDepth + ((F == W_CBF16) ? kMetaRing : 0);
 };
 
+// One weight matrix of a launch. Several matrices that share x and K (the
+// projections that read the same activations) can run in one launch; their rows
+// are concatenated: segment s owns launch rows [row0, next row0).
+constexpr int kMaxSegs = 8;
+struct Segment {
+  const void* w;    // weights, codes or coded payload
+  const void* aux;  // coded metadata (u32) / scales
+  void* out;        // out[t * ldo + local row]
+  int ldo;
+  int row0;         // first launch row of this segment
+};
+
 struct GemvParams {
   const void* x;        // [M, ldx] activations (X format)
-  const void* w;        // weights, codes or coded payload
-  const void* aux;      // coded metadata (u32) / scales
   const float* gscale;  // W_FP4_G16E global scale (device scalar)
-  void* out;            // out[t * ldo + row]
+  Segment seg[kMaxSegs];
+  int nseg;
   float* ws;            // split mode: partials [tiles*MT][N][S]
   unsigned* tickets;    // split mode: [tiles][N], zero between launches
   int* status;          // device status word
-  int m, n, k;
-  int ldx, ldo;
+  int m, n, k;          // n: total rows over all segments
+  int ldx;
   int out_f32;
   int split;      // 0: rows dealt to CTAs; 1: items dealt to CTAs (split-K)
   int use_tma;    // 1: bulk copies; 0: cooperative loads (any alignment)
   int chunks;     // S = ceil(K / KC)
 };
+
+// Segment of a launch row and the row's index inside that segment.
+struct RowRef {
+  const char* w;
+  const char* aux;
+  int local;
+  int seg;
+};
+
+__device__ __forceinline__ RowRef resolve_row(const GemvParams& p, int row) {
+  int s = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxSegs; ++i)
+    if (i < p.nseg && row >= p.seg[i].row0) s = i;
+  return RowRef{static_cast<const char*>(p.seg[s].w), static_cast<const char*>(p.seg[s].aux),
+                row - p.seg[s].row0, s};
+}
 
 // ------------------------------------------------------------------ x staging
 
@@ -491,17 +519,16 @@ __device__ __forceinline__ long long w_offset_bytes(long long elem) {
 
 // Scale bytes of (row, chunk c) covering L columns; source pointer and byte count.
 template <int F>
-__device__ __forceinline__ void scale_span(const GemvParams& p, int row, int c, int L,
-                                           const char** src, int* bytes) {
+__device__ __forceinline__ void scale_span(const RowRef& r, int k, int c, int L, const char** src, int* bytes) {
   constexpr int KC = Layout<F>::KC;
   if constexpr (F == W_I8_G64) {
-    *src = static_cast<const char*>(p.aux) + (static_cast<long long>(row) * (p.k / 64) + c * (KC / 64)) * 4;
+    *src = r.aux + (static_cast<long long>(r.local) * (k / 64) + c * (KC / 64)) * 4;
     *bytes = (L / 64) * 4;
   } else if constexpr (F == W_FP4_G32H) {
-    *src = static_cast<const char*>(p.aux) + (static_cast<long long>(row) * (p.k / 32) + c * (KC / 32)) * 2;
+    *src = r.aux + (static_cast<long long>(r.local) * (k / 32) + c * (KC / 32)) * 2;
     *bytes = (L / 32) * 2;
   } else if constexpr (F == W_FP4_G16E) {
-    *src = static_cast<const char*>(p.aux) + (static_cast<long long>(row) * (p.k / 16) + c * (KC / 16));
+    *src = r.aux + (static_cast<long long>(r.local) * (k / 16) + c * (KC / 16));
     *bytes = L / 16;
   } else {
     *src = nullptr;
@@ -538,15 +565,16 @@ struct Cursor {
 };
 
 template <int F, int MT>
-__device__ __forceinline__ void finalize_token(const GemvParams& p, int row, int token, float v,
+__device__ __forceinline__ void finalize_token(const GemvParams& p, const RowRef& r, int token, float v,
                                                float row_scale) {
   if constexpr (F == W_I8_ROW) v = mul_rn(v, row_scale);
   if constexpr (F == W_FP4_G16E) v = mul_rn(v, __ldg(p.gscale));
-  const long long idx = static_cast<long long>(token) * p.ldo + row;
+  const Segment& sg = p.seg[r.seg];
+  const long long idx = static_cast<long long>(token) * sg.ldo + r.local;
   if (p.out_f32) {
-    static_cast<float*>(p.out)[idx] = v;
+    static_cast<float*>(sg.out)[idx] = v;
   } else {
-    static_cast<unsigned short*>(p.out)[idx] = f32_to_bf16_rn(v);
+    static_cast<unsigned short*>(sg.out)[idx] = f32_to_bf16_rn(v);
   }
 }
 
@@ -602,7 +630,8 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
   auto issue_meta = [&](int ix, const Cursor& m) {
     const int nb = min(32, k / 64 - 32 * m.c);
     const unsigned bar = mbar0 + (ix % kMetaRing) * 8;
-    const char* src = static_cast<const char*>(p.aux) + (static_cast<long long>(m.row) * (k / 64) + 32 * m.c) * 4;
+    const RowRef r = resolve_row(p, m.row);
+    const char* src = r.aux + (static_cast<long long>(r.local) * (k / 64) + 32 * m.c) * 4;
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(bar, nb * 4);
     bulk_g2s(meta0 + (ix % kMetaRing) * kMetaEntry, src, nb * 4, bar);
@@ -616,18 +645,19 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
     int bytes;
     const char* ssrc = nullptr;
     int sbytes = 0;
+    const RowRef r = resolve_row(p, it.row);
     if constexpr (CODED) {
       const unsigned entry = meta0 + (ix % kMetaRing) * kMetaEntry;
       const int nb = L / 64;
       const unsigned m0 = lds32(entry), ml = lds32(entry + 4 * (nb - 1));
       const unsigned off = (m0 & 0x7fffffu) << 5;
       const unsigned end = ((ml & 0x7fffffu) << 5) + ((ml >> 31) ? 128u : 96u);
-      src = static_cast<const char*>(p.w) + off;
+      src = r.w + off;
       bytes = static_cast<int>(end - off);
     } else {
-      src = static_cast<const char*>(p.w) + w_offset_bytes<F>(static_cast<long long>(it.row) * k + it.c * KC);
+      src = r.w + w_offset_bytes<F>(static_cast<long long>(r.local) * k + it.c * KC);
       bytes = static_cast<int>(w_offset_bytes<F>(L));
-      scale_span<F>(p, it.row, it.c, L, &ssrc, &sbytes);
+      scale_span<F>(r, k, it.c, L, &ssrc, &sbytes);
     }
     fence_proxy_async_smem();
     mbar_arrive_expect_tx(bar, bytes + sbytes);
@@ -686,6 +716,7 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
 #pragma unroll
   for (int t = 0; t < MT; ++t) rowsum[t] = 0.0f;
   float row_scale = 1.0f;
+  RowRef rref = resolve_row(p, cur.row);
   bool row_complete = true;
   int contributed = 0;
 
@@ -693,6 +724,7 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
   for (; q < nitems && ok; ++q) {
     const int row = cur.row, c = cur.c;
     const int L = min(KC, k - c * KC);
+    if (c == 0 || q == 0) rref = resolve_row(p, row);
     const unsigned slot = slot0 + (q % kDepth) * SLOT;
     const unsigned entry = meta0 + (q % kMetaRing) * kMetaEntry;
     if (p.use_tma) {
@@ -721,21 +753,21 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
         unsigned* ep = reinterpret_cast<unsigned*>(slot0_ptr + kDepth * SLOT + (q % kMetaRing) * kMetaEntry);
         const int nb = L / 64;
         if (lane < nb)
-          ep[lane] = __ldg(static_cast<const unsigned*>(p.aux) + static_cast<long long>(row) * (k / 64) + 32 * c + lane);
+          ep[lane] = __ldg(reinterpret_cast<const unsigned*>(rref.aux) + static_cast<long long>(rref.local) * (k / 64) +
+                           32 * c + lane);
         __syncwarp();
         const unsigned m0 = ep[0], ml = ep[nb - 1];
         const unsigned off = (m0 & 0x7fffffu) << 5;
         const unsigned end = ((ml & 0x7fffffu) << 5) + ((ml >> 31) ? 128u : 96u);
-        warp_copy_bytes(reinterpret_cast<char*>(sp), static_cast<const char*>(p.w) + off,
-                        static_cast<int>(end - off), kWeightSlot, lane);
+        warp_copy_bytes(reinterpret_cast<char*>(sp), rref.w + off, static_cast<int>(end - off), kWeightSlot, lane);
       } else {
-        const char* src = static_cast<const char*>(p.w) + w_offset_bytes<F>(static_cast<long long>(row) * k + c * KC);
+        const char* src = rref.w + w_offset_bytes<F>(static_cast<long long>(rref.local) * k + c * KC);
         warp_copy_bytes(reinterpret_cast<char*>(sp), src, static_cast<int>(w_offset_bytes<F>(L)),
                         kWeightSlot, lane);
         if constexpr (WTraits<F>::SCALE_BYTES > 0) {
           const char* ssrc;
           int sbytes;
-          scale_span<F>(p, row, c, L, &ssrc, &sbytes);
+          scale_span<F>(rref, k, c, L, &ssrc, &sbytes);
           warp_copy_bytes(reinterpret_cast<char*>(sp) + kWeightSlot, ssrc, sbytes, WTraits<F>::SCALE_BYTES,
                           lane);
         }
@@ -744,7 +776,7 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
     }
 
     if (c == 0 || q == 0) {
-      if constexpr (F == W_I8_ROW) row_scale = __ldg(static_cast<const float*>(p.aux) + row);
+      if constexpr (F == W_I8_ROW) row_scale = __ldg(reinterpret_cast<const float*>(rref.aux) + rref.local);
       if (p.split)
         row_complete = static_cast<long long>(row) * S >= wbegin && static_cast<long long>(row) * S + S <= wend;
     }
@@ -767,7 +799,7 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
           const int token = tile * MT + t;
-          if (lane == t && token < p.m) finalize_token<F, MT>(p, row, token, rowsum[t], row_scale);
+          if (lane == t && token < p.m) finalize_token<F, MT>(p, rref, token, rowsum[t], row_scale);
         }
       }
     } else {
@@ -797,7 +829,7 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
               const float* src = p.ws + ((static_cast<long long>(tile) * MT + t) * n + row) * S;
               float total = __ldcg(src);
               for (int cc = 1; cc < S; ++cc) total = add_rn(total, __ldcg(src + cc));
-              finalize_token<F, MT>(p, row, token, total, row_scale);
+              finalize_token<F, MT>(p, rref, token, total, row_scale);
             }
           }
           if (lane == 0) *ticket = 0u;

@@ -402,3 +402,53 @@ def test_prefetch_never_writes_and_driver_abi_path():
     torch.cuda.synchronize()
     assert torch.equal(t, before)
     assert int(sink.item()) == 0
+
+
+# ---------------------------------------------------------------- multi-segment launches / chain
+
+@pytest.mark.parametrize("m,split", [(1, 0), (1, 1), (3, 0)])
+def test_multi_segment_equals_separate_launches(native, m, split):
+    from klab_b200 import _native as nat
+    from klab_b200 import compressed_bf16 as cb
+
+    options(native, split, 0)
+    k = 6144
+    sizes = (96, 32, 8, 200)
+    ws = [dev_bf16(og.normal_bf16_bits(40 + i, (n, k), 0.02)) for i, n in enumerate(sizes)]
+    x = dev_bf16(og.normal_bf16_bits(50, (m, k), 1.0))
+    full = torch.zeros((m, sum(sizes) + 5), dtype=torch.bfloat16, device="cuda")
+    segments, col = [], 0
+    for w, n in zip(ws, sizes):
+        segments.append((w, None, full[:, col:], full.shape[1], n))
+        col += n
+    nat.gemv_multi(nat.W_BF16, nat.DT_BF16, x, segments, None, nat.DT_BF16, m, k)
+    col = 0
+    for w, n in zip(ws, sizes):
+        alone = cb.raw_linear(x, w, threads=128, vector=8, output_dtype="bf16")
+        assert same_bits(full[:, col:col + n].contiguous(), alone)
+        col += n
+    assert not full[:, col:].any()
+
+
+def test_chain_fused_equals_unfused_and_graph():
+    from klab_b200.chain import ChainShape, ProjectionChain
+
+    shape = ChainShape(layers=3, hidden=512, kv=128, ffn=1536)
+    x = dev_bf16(og.normal_bf16_bits(60, (1, 512), 1.0))
+    fused = ProjectionChain(shape, seed=3, fuse=True)
+    plain = ProjectionChain(shape, seed=3, fuse=False)
+    a = fused.forward_eager(x).clone()
+    b = plain.forward_eager(x).clone()
+    assert same_bits(a, b)
+    out = fused.capture(x)
+    fused.replay()
+    torch.cuda.synchronize()
+    assert same_bits(out, a)
+    # one layer against the oracle (up, then down, each rounded once to BF16)
+    one = ProjectionChain(ChainShape(layers=1, hidden=512, kv=128, ffn=1536), seed=3)
+    got = host_bits(one.forward_eager(x))
+    entry = one.layers[0]
+    up = ob.round_bf16_bits(og.bf16_projection64(host_bits(x), host_bits(entry["up"][0])))
+    ref64 = og.bf16_projection64(up, host_bits(entry["down"][0]))
+    report = ob.check_outputs(ref64, ob.bf16_values(got), output_dtype="bf16")
+    assert report["passed"] and report["max_ulp_error"] <= 1, report
