@@ -72,6 +72,7 @@ extern "C" {
 #define KLAB_E_ALIGN (-2002)       /* pointer/stride alignment not supported */
 #define KLAB_E_UNSUPPORTED (-2003) /* dtype/format combination not supported */
 #define KLAB_E_DEVICE (-2004)      /* a kernel recorded a device-side error (bounded wait expired) */
+#define KLAB_E_SCRATCH (-2005)     /* the shape needs more than the library's static 4 MiB scratch */
 
 /* Options (klab_set_option). */
 #define KLAB_OPT_PDL 0        /* 1 (default): launch with programmatic dependent launch */
@@ -143,6 +144,18 @@ KLAB_API int klab_int8_linear(const void* x, int xdtype, const int8_t* codes, co
 KLAB_API int klab_fp4_linear(const void* x, int xdtype, const uint8_t* packed, const void* scales,
                     int scale_kind, const float* gscale, void* out, int out_dtype, int m, int n, int k,
                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* klab_raw_linear without any allocation, for callers that cannot allocate
+ * device memory (no framework allocator, a host application that owns all
+ * device memory, a fixed-footprint process). Split-K scratch comes from a
+ * static 4 MiB array inside the library (held by every GPU that loads it);
+ * shapes whose scratch need (klab_gemv_workspace_bytes) exceeds 4 MiB return
+ * KLAB_E_SCRATCH. The first call on a device looks up the array's address:
+ * make it before any CUDA graph capture. Calls share the array: calls whose
+ * kernels can overlap on the GPU race and must be serialized by the caller.
+ * No counterpart in the reference (its kernels have no workspace). */
+KLAB_API int klab_raw_linear_noalloc(const void* x, const void* w, void* out, int out_dtype, int m, int n, int k,
+                                     void* stream);
 
 /* Workspace bytes a klab_gemv call of this shape can use for split-K (0 = none);
  * for klab_gemv_multi pass the total row count as n. */

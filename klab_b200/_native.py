@@ -26,7 +26,7 @@ FP4_E4M3_G16, FP4_F16_G32 = 0, 1
 L2_HINT, L2_HINT_LAST, L2_LOAD = 0, 1, 2
 OPT_PDL, OPT_SPLIT, OPT_GENERIC, OPT_CTAS_PER_SM = 0, 1, 2, 3
 E_DRIVER, E_NO_CONTEXT, E_INVALID = -1000, -1001, -1002
-E_SHAPE, E_ALIGN, E_UNSUPPORTED, E_DEVICE = -2001, -2002, -2003, -2004
+E_SHAPE, E_ALIGN, E_UNSUPPORTED, E_DEVICE, E_SCRATCH = -2001, -2002, -2003, -2004, -2005
 
 _P = ct.c_void_p
 _I = ct.c_int
@@ -35,6 +35,7 @@ _SIGNATURES = {
     "klab_gemv": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "klab_gemv_multi": (_I, [_I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "klab_raw_linear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_raw_linear_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "klab_coded_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     "klab_half_linear": (_I, [_P, _P, _I, _P, _I, _I, _I, _P, _SZ, _P]),
     "klab_f32_linear": (_I, [_P, _P, _P, _I, _I, _I, _P, _SZ, _P]),

@@ -464,6 +464,7 @@ const char* klab_error_string(int code) {
     case KLAB_E_ALIGN: return "Pointer or stride alignment not supported";
     case KLAB_E_UNSUPPORTED: return "Unsupported dtype or format combination";
     case KLAB_E_DEVICE: return "A kernel recorded a device-side error (bounded wait expired)";
+    case KLAB_E_SCRATCH: return "Shape needs more split-K scratch than the library's static 4 MiB array";
     default:
       if (code > 0) return cudaGetErrorString(static_cast<cudaError_t>(code));
       return "Unknown klab error";
