@@ -382,7 +382,10 @@ def main(argv=None):
     parser.add_argument("--no-projections", action="store_true", help="skip the per-config projection lines")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--quick", action="store_true", help="fewer rounds and shapes (smoke runs)")
-    parser.add_argument("--gather", choices=("nccl",), default="nccl")
+    parser.add_argument("--gather", choices=("nccl", "p2p"), default="p2p",
+                        help="N>1: NCCL all-gathers, or gathers fused into the projections over NVLink")
+    parser.add_argument("--persistent", action=argparse.BooleanOptionalAction, default=False,
+                        help="the whole token step as one persistent kernel launch")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -410,7 +413,8 @@ def main(argv=None):
 
     peak, peak_kind = measured_peak()
     shape = ChainShape(layers=args.layers)
-    chain = ProjectionChain(shape, rank=rank, world=world, group=group, seed=0)
+    chain = ProjectionChain(shape, rank=rank, world=world, group=group, seed=0, gather=args.gather,
+                            persistent=args.persistent)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(1234)
     x = torch.randn((1, shape.hidden), generator=gen, device="cuda").to(torch.bfloat16)
@@ -459,6 +463,7 @@ def main(argv=None):
     t3 = time.perf_counter()
     e2e_s = all_max(torch, t3 - t2, world)
 
+    launches = chain.launches_per_step()
     roofline = bench_dominant_kernel(torch, chain, peak)
     roofline["peak_kind"] = peak_kind
     status = _native.device_status(clear=True)
@@ -483,11 +488,14 @@ def main(argv=None):
             "data": "synthetic (seeded N(0,0.02^2) bf16 weights, N(0,1) bf16 token)",
             "config": {"workload": "c5_chain_llama3_8b_shapes_32_layers_m1", "layers": shape.layers, "M": 1,
                        "hidden": shape.hidden, "ffn": shape.ffn, "kv": shape.kv,
-                       "parallelism": f"column-shard x{world}" + (" + nccl all-gather" if world > 1 else ""),
+                       "parallelism": f"column-shard x{world}" + (
+                           {"nccl": " + nccl all-gather", "p2p": " + all-gather fused into the projections "
+                            "(NVLink peer stores)"}[args.gather] if world > 1 else ""),
                        "bytes_per_token": shape.bytes_per_token(),
                        "l2": "weights 13.96 GB per step >> 126 MB L2 (no flush needed)",
-                       "graph": "one CUDA graph per token step, PDL launches"},
-            "gpu_launches": args.steps * 7 * shape.layers,
+                       "graph": ("one CUDA graph per token step: input copy + one persistent chain kernel"
+                                 if args.persistent else "one CUDA graph per token step, PDL launches")},
+            "gpu_launches": args.steps * launches,
             "hbm_gbs_per_gpu": round(shape.bytes_per_token() / world * value / 1e9, 1),
             "roofline": roofline,
             "e2e": {"value": round(e2e_steps / e2e_s, 2), "unit": "tok/s",

@@ -102,6 +102,91 @@ KLAB_API int klab_gemv_multi(int wfmt, int xdtype, const void* x, int ldx, int n
                              const int* n, int out_dtype, int m, int k, void* workspace, size_t workspace_bytes,
                              void* stream);
 
+/* Output gather fused into a projection, over NVLink peer memory (no
+ * counterpart in the reference, which has no multi-GPU code; it replaces the
+ * per-layer NCCL all-gather of the sharded chain). Segment `seg`'s outputs are
+ * also stored into each rank's copy of its output buffer (peer_out, mapped with
+ * klab_ipc_open); after the grid, this rank's flag (slot signal_slot) is raised
+ * to *epoch on every rank. With wait_flags set, the launch first waits
+ * (bounded) until all npeers flags of wait_slot reach *epoch before reading x.
+ * Flag arrays are [slots][npeers] u32, monotonic, zero at start. `done` is a
+ * device word that is zero between launches. */
+typedef struct klab_gather {
+  int npeers;
+  int rank;
+  int seg;
+  void* peer_out[8];
+  unsigned* peer_flags[8];
+  int signal_slot;
+  const unsigned* wait_flags;
+  int wait_slot;
+  const unsigned* epoch;
+  unsigned* done;
+} klab_gather_t;
+
+/* klab_gemv_multi with a fused output gather (gather may be NULL). */
+KLAB_API int klab_gemv_multi_gather(int wfmt, int xdtype, const void* x, int ldx, int nseg, const void* const* w,
+                                    const void* const* aux, const float* gscale, void* const* out, const int* ldo,
+                                    const int* n, int out_dtype, int m, int k, const klab_gather_t* gather,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Peer memory for the fused gather (CUDA IPC, one node): allocate a zero-filled
+ * buffer and its 64-byte IPC handle; map a peer's handle; unmap; free. */
+KLAB_API int klab_ipc_malloc(size_t bytes, void** ptr, void* handle64);
+KLAB_API int klab_ipc_open(const void* handle64, void** ptr);
+KLAB_API int klab_ipc_close(void* ptr);
+KLAB_API int klab_ipc_free(void* ptr);
+/* Start a gathered step: *epoch += 1 on `stream` (one thread). */
+KLAB_API int klab_step_begin(unsigned* epoch, void* stream);
+/* Wait (bounded, on the device) until all npeers flags of `slot` reach *epoch. */
+KLAB_API int klab_wait_flags(const unsigned* flags, int slot, int npeers, const unsigned* epoch, void* stream);
+
+/* Persistent projection chain (no counterpart in the reference, whose chain is
+ * one launch per projection, l2prefetch.py:38-60): every projection of a token
+ * step in ONE cooperative launch, BF16 weights, one token. Stage s computes
+ * the rows of its nseg weights w[i] [n[i], k] from the input x. Segment
+ * gather_seg feeds the next stage: its outputs are written as 32-bit words
+ * (tag << 16 | bf16) into every rank's gather buffer (peer_out[q], rank q's
+ * buffer at this rank's first row; peer_out[rank] is the local one), over
+ * NVLink for the peers. Stage 0's x is plain BF16; stage s > 0's x is the
+ * local gather buffer of stage s-1 (tagged words, n[gather_seg] * npeers of
+ * them). Other segments write plain BF16 to out[i]. Gather buffers start
+ * zeroed. sync->final_in is the last stage's local gather buffer; the launch
+ * ends after its plain BF16 values are in final_out. epoch (device u32, zero at
+ * start) counts completed steps. Outputs are bit-identical to one
+ * klab_gemv_multi launch per stage. One GPU: npeers = 1. */
+typedef struct klab_chain_stage {
+  const void* x;
+  int k;
+  int nseg;
+  const void* w[8];
+  void* out[8];
+  int n[8];
+  int gather_seg;
+  void* peer_out[8];
+} klab_chain_stage_t;
+
+typedef struct klab_chain_sync {
+  int npeers;
+  int rank;
+  unsigned* epoch;
+  const unsigned* final_in;
+  void* final_out;
+} klab_chain_sync_t;
+
+/* Validate the stages once and upload them (call outside graph capture). */
+KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, const klab_chain_sync_t* sync,
+                               void** plan);
+/* One token step: a single kernel launch on `stream` (capturable). */
+KLAB_API int klab_chain_launch(void* plan, void* stream);
+KLAB_API int klab_chain_destroy(void* plan);
+/* Launch shape of a plan: CTAs and trace slots per (stage, CTA). */
+KLAB_API int klab_chain_info(void* plan, int* grid, int* trace_slots);
+/* Optional timeline: later launches write global-timer ns per (stage, CTA):
+ * [entered, x staged, then each warp's last item] into buffer
+ * [nstages][grid][trace_slots] u64 (NULL: off). */
+KLAB_API int klab_chain_trace(void* plan, unsigned long long* buffer, size_t bytes);
+
 /* BF16 x, raw BF16 W, BF16 or FP32 out.
  * Replaces compressed_bf16.raw_linear (compressed_bf16.py:450-460, kernels
  * cbf16_raw_{bf16,fp32}_t*_v*, compressed_kernels.cu:156-176) and

@@ -34,6 +34,18 @@ _SZ = ct.c_size_t
 _SIGNATURES = {
     "klab_gemv": (_I, [_I, _I, _P, _I, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _SZ, _P]),
     "klab_gemv_multi": (_I, [_I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
+    "klab_gemv_multi_gather": (_I, [_I, _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _I, _P, _P, _SZ, _P]),
+    "klab_ipc_malloc": (_I, [_SZ, ct.POINTER(_P), _P]),
+    "klab_ipc_open": (_I, [_P, ct.POINTER(_P)]),
+    "klab_ipc_close": (_I, [_P]),
+    "klab_ipc_free": (_I, [_P]),
+    "klab_step_begin": (_I, [_P, _P]),
+    "klab_chain_create": (_I, [_P, _I, _P, ct.POINTER(_P)]),
+    "klab_chain_launch": (_I, [_P, _P]),
+    "klab_chain_destroy": (_I, [_P]),
+    "klab_chain_info": (_I, [_P, ct.POINTER(_I), ct.POINTER(_I)]),
+    "klab_chain_trace": (_I, [_P, _P, _SZ]),
+    "klab_wait_flags": (_I, [_P, _I, _I, _P, _P]),
     "klab_raw_linear": (_I, [_P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     "klab_raw_linear_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "klab_coded_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
@@ -195,9 +207,112 @@ def gemv(wfmt, xdt, x, w, aux, gscale, out, out_dt, m, n, k, *, ldx=None, ldo=No
     return out
 
 
-def gemv_multi(wfmt, xdt, x, segments, gscale, out_dt, m, k, *, ldx=None, workspace=True):
+MAX_PEERS = 8
+
+
+class Gather(ct.Structure):
+    """klab_gather_t: an output gather fused into a projection (peer stores plus
+    a completion flag), and/or a bounded wait for the peers' flags before x is read."""
+
+    _fields_ = [("npeers", _I), ("rank", _I), ("seg", _I), ("peer_out", _P * MAX_PEERS),
+                ("peer_flags", _P * MAX_PEERS), ("signal_slot", _I), ("wait_flags", _P), ("wait_slot", _I),
+                ("epoch", _P), ("done", _P)]
+
+
+def make_gather(npeers, rank, epoch, *, seg=-1, peer_out=(), peer_flags=(), signal_slot=-1, wait_flags=None,
+                wait_slot=-1, done=None):
+    """A Gather from raw device addresses (ints)."""
+    g = Gather()
+    g.npeers, g.rank, g.seg = npeers, rank, seg
+    for q, a in enumerate(peer_out):
+        g.peer_out[q] = a
+    for q, a in enumerate(peer_flags):
+        g.peer_flags[q] = a
+    g.signal_slot, g.wait_flags, g.wait_slot = signal_slot, wait_flags, wait_slot
+    g.epoch, g.done = epoch, done
+    return g
+
+
+class ChainStage(ct.Structure):
+    """klab_chain_stage_t: one stage of the persistent chain kernel."""
+
+    _fields_ = [("x", _P), ("k", _I), ("nseg", _I), ("w", _P * 8), ("out", _P * 8), ("n", _I * 8),
+                ("gather_seg", _I), ("peer_out", _P * MAX_PEERS)]
+
+
+class ChainSync(ct.Structure):
+    """klab_chain_sync_t: ranks, step counter and the step output of a chain."""
+
+    _fields_ = [("npeers", _I), ("rank", _I), ("epoch", _P), ("final_in", _P), ("final_out", _P)]
+
+
+def chain_create(stages, sync) -> int:
+    """Upload a persistent chain plan; stages is a list of ChainStage."""
+    arr = (ChainStage * len(stages))(*stages)
+    plan = ct.c_void_p()
+    check(lib().klab_chain_create(arr, len(stages), ct.byref(sync), ct.byref(plan)), "klab_chain_create")
+    return plan.value
+
+
+def chain_launch(plan: int, stream) -> None:
+    check(lib().klab_chain_launch(plan, stream.cuda_stream), "klab_chain_launch")
+
+
+def chain_info(plan: int):
+    """(CTAs per launch, trace slots per (stage, CTA)) of a chain plan."""
+    grid, slots = ct.c_int(), ct.c_int()
+    check(lib().klab_chain_info(plan, ct.byref(grid), ct.byref(slots)), "klab_chain_info")
+    return grid.value, slots.value
+
+
+def chain_trace(plan: int, buffer) -> None:
+    """Record a timeline into `buffer` (int64 CUDA tensor, or None to stop)."""
+    if buffer is None:
+        check(lib().klab_chain_trace(plan, None, 0), "klab_chain_trace")
+    else:
+        check(lib().klab_chain_trace(plan, buffer.data_ptr(), buffer.numel() * buffer.element_size()),
+              "klab_chain_trace")
+
+
+def chain_destroy(plan: int) -> None:
+    check(lib().klab_chain_destroy(plan), "klab_chain_destroy")
+
+
+def ipc_malloc(nbytes: int):
+    """Zero-filled device memory on the current device and its 64-byte IPC handle."""
+    p = ct.c_void_p()
+    handle = ct.create_string_buffer(64)
+    check(lib().klab_ipc_malloc(nbytes, ct.byref(p), handle), "klab_ipc_malloc")
+    return p.value, handle.raw
+
+
+def ipc_open(handle: bytes) -> int:
+    p = ct.c_void_p()
+    buf = ct.create_string_buffer(bytes(handle), 64)
+    check(lib().klab_ipc_open(buf, ct.byref(p)), "klab_ipc_open")
+    return p.value
+
+
+def ipc_close(address: int) -> None:
+    check(lib().klab_ipc_close(address), "klab_ipc_close")
+
+
+def ipc_free(address: int) -> None:
+    check(lib().klab_ipc_free(address), "klab_ipc_free")
+
+
+def step_begin(epoch, stream) -> None:
+    check(lib().klab_step_begin(epoch.data_ptr(), stream.cuda_stream), "klab_step_begin")
+
+
+def wait_flags(flags: int, slot: int, npeers: int, epoch, stream) -> None:
+    check(lib().klab_wait_flags(flags, slot, npeers, epoch.data_ptr(), stream.cuda_stream), "klab_wait_flags")
+
+
+def gemv_multi(wfmt, xdt, x, segments, gscale, out_dt, m, k, *, ldx=None, workspace=True, gather=None):
     """One launch over several projections sharing x: segments is a list of
-    (w, aux, out_view, ldo, n_rows); out_view points at the first output element."""
+    (w, aux, out_view, ldo, n_rows); out_view points at the first output element.
+    gather (a Gather) fuses an output push to the peers and/or a wait for them."""
     import torch
 
     nseg = len(segments)
@@ -211,8 +326,13 @@ def gemv_multi(wfmt, xdt, x, segments, gscale, out_dt, m, k, *, ldx=None, worksp
     ldo = (ct.c_int * nseg)(*[seg[3] for seg in segments])
     ns = (ct.c_int * nseg)(*[seg[4] for seg in segments])
     with torch.cuda.device(device):
-        rc = lib().klab_gemv_multi(wfmt, xdt, x.data_ptr(), k if ldx is None else ldx, nseg, wp, ap,
-                                   None if gscale is None else gscale.data_ptr(), op, ldo, ns, out_dt, m, k,
-                                   ws_ptr, ws_bytes, stream.cuda_stream)
+        if gather is None:
+            rc = lib().klab_gemv_multi(wfmt, xdt, x.data_ptr(), k if ldx is None else ldx, nseg, wp, ap,
+                                       None if gscale is None else gscale.data_ptr(), op, ldo, ns, out_dt, m, k,
+                                       ws_ptr, ws_bytes, stream.cuda_stream)
+        else:
+            rc = lib().klab_gemv_multi_gather(wfmt, xdt, x.data_ptr(), k if ldx is None else ldx, nseg, wp, ap,
+                                              None if gscale is None else gscale.data_ptr(), op, ldo, ns, out_dt,
+                                              m, k, ct.byref(gather), ws_ptr, ws_bytes, stream.cuda_stream)
     check(rc, "klab_gemv_multi")
     record(stream, x, *[t for seg in segments for t in (seg[0], seg[1], seg[2])])

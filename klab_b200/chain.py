@@ -13,8 +13,14 @@ sharded chain is bit-identical to the one-GPU chain. The whole token step is
 captured in one CUDA graph; launches use programmatic dependent launch so a
 projection's weight stream starts while the previous one drains.
 
-The reference has no distributed code (its chain is single-GPU); the
-all-gather is NCCL through torch.distributed.
+The reference has no distributed code (its chain is single-GPU). Two gather
+modes: "nccl" (all_gather_into_tensor through torch.distributed after each
+gathered projection) and "p2p", where the gather is fused into the projection
+kernel: its epilogue also stores every output value into each peer's copy of
+the gather buffer over NVLink (CUDA IPC mappings), the grid's last CTA raises
+this rank's flag on every rank, and the next projection waits (bounded, on the
+device) for all flags of that slot before reading its input. Flags carry the
+step's epoch, so they never need resetting; see p2p_schedule for the slots.
 """
 
 from __future__ import annotations
@@ -57,6 +63,30 @@ def _shard(n, rank, world):
     return rank * part, (rank + 1) * part
 
 
+def p2p_schedule(layers):
+    """Flag slots of one step in "p2p" mode, as a list of launches
+    (kind, layer, wait_slot, signal_slot): stage A of layer i signals slot 2i
+    (its up output is gathered) and waits for slot 2i-1 (the previous down
+    output, its input); down of layer i waits for 2i and signals 2i+1; the step
+    ends with a wait on slot 2*layers-1. wait_slot -1: no wait (layer 0 reads
+    the step input, which is local)."""
+    out = []
+    for i in range(layers):
+        out.append(("stage_a", i, 2 * i - 1 if i else -1, 2 * i))
+        out.append(("down", i, 2 * i, 2 * i + 1))
+    out.append(("end", layers, 2 * layers - 1, -1))
+    return out
+
+
+class _DeviceBytes:
+    """A raw device allocation seen by torch through __cuda_array_interface__
+    (the memory is owned and freed by the chain)."""
+
+    def __init__(self, address, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (address, False),
+                                         "version": 3, "strides": None}
+
+
 def make_weight(shape, layer, name, rows, device, std=0.02, seed=0):
     """Deterministic N(0, std^2) BF16 weight rows [r0, r1) of projection `name` in
     `layer`: the full matrix is generated from one seed and sliced, so every
@@ -75,10 +105,27 @@ class ProjectionChain:
     process group (NCCL) when world > 1."""
 
     def __init__(self, shape: ChainShape = ChainShape(), *, rank=0, world=1, device=None, group=None,
-                 seed=0, std=0.02, weights=None, project=None, fuse=True):
+                 seed=0, std=0.02, weights=None, project=None, fuse=True, gather="nccl", persistent=False):
         """weights(layer, name, rows) -> BF16 tensor supplies shard weights (default:
         seeded N(0, std^2)); project(x, w, n_rows, k, out, ldo) replaces the native
-        projection (host-side tests drive the sharding and gathers on CPU with it)."""
+        projection (host-side tests drive the sharding and gathers on CPU with it).
+        gather: "nccl" or "p2p" (fused peer stores; needs the native fused path).
+        persistent: the whole step is one launch of the persistent chain kernel
+        (one token; with world > 1 it needs gather="p2p")."""
+        if gather not in ("nccl", "p2p"):
+            raise ValueError(f"gather must be 'nccl' or 'p2p', not {gather!r}")
+        if gather == "p2p" and (project is not None or not fuse):
+            raise ValueError("gather='p2p' needs the native projection with fuse=True")
+        if persistent and (project is not None or not fuse or shape.tokens != 1
+                           or (world > 1 and gather != "p2p")):
+            raise ValueError("persistent=True needs the native projection, fuse=True, one token and, "
+                             "with several ranks, gather='p2p'")
+        self.persistent = persistent
+        self._plan = None
+        if world > 8 and gather == "p2p":
+            raise ValueError("gather='p2p' supports at most 8 ranks")
+        self.gather = gather if world > 1 else "none"
+        self._ipc = None
         self.shape = shape
         self.rank, self.world, self.group = rank, world, group
         if project is None:
@@ -108,17 +155,156 @@ class ProjectionChain:
         bf = dict(dtype=torch.bfloat16, device=self.device)
         # Two full-width layer-input buffers used alternately: layer i reads
         # hbuf[i % 2] and its down projection (and gather) writes hbuf[(i+1) % 2].
-        self.hbuf = [torch.zeros((m, shape.hidden), **bf) for _ in range(2)]
         self.a_out = {name: torch.zeros((m, n), **bf) for name, n in stage_a if name not in ("up",)}
-        self.up_full = torch.zeros((m, shape.ffn), **bf)       # gather buffer for up
+        if self.persistent:
+            pass                                                   # buffers: _setup_persistent
+        elif self.gather == "p2p":
+            self._setup_p2p()
+        else:
+            self.hbuf = [torch.zeros((m, shape.hidden), **bf) for _ in range(2)]
+            self.up_full = torch.zeros((m, shape.ffn), **bf)       # gather buffer for up
         self.graph = None
         self.stream = torch.cuda.Stream(self.device) if self.device.type == "cuda" else None
+        if self.persistent:
+            self._setup_persistent()
+
+    def _setup_persistent(self):
+        """Stage table of the persistent kernel: stage 2i = the six stage-A
+        projections of layer i (up feeds stage 2i+1), stage 2i+1 = down (feeds
+        the next layer). The up and down outputs live only as tagged words
+        (tag << 16 | bf16) in the gather buffers up_t [ffn] and h_t [hidden],
+        which every rank writes into (IPC mappings when world > 1)."""
+        shape, world, rank = self.shape, self.world, self.rank
+        bf = dict(dtype=torch.bfloat16, device=self.device)
+        self.hbuf = [torch.zeros((1, shape.hidden), **bf)]        # step input (plain BF16)
+        self.out = torch.zeros((1, shape.hidden), **bf)           # step output (plain BF16)
+        self.up_full = None
+        words = {"ht": shape.hidden * 4, "upt": shape.ffn * 4}
+        if world == 1:
+            self.h_t = torch.zeros(shape.hidden, dtype=torch.int32, device=self.device)
+            self.up_t = torch.zeros(shape.ffn, dtype=torch.int32, device=self.device)
+            bases = {"ht": [self.h_t.data_ptr()], "upt": [self.up_t.data_ptr()]}
+        else:
+            raw, offsets = self._ipc_region(words)
+            self.h_t = raw[offsets["ht"]:offsets["ht"] + words["ht"]].view(torch.int32)
+            self.up_t = raw[offsets["upt"]:offsets["upt"] + words["upt"]].view(torch.int32)
+            bases = {name: [a + offsets[name] for a in self._ipc["peers"]] for name in words}
+        self.ctrl = torch.zeros(64, dtype=torch.int32, device=self.device)
+        self.epoch = self.ctrl[0:1]
+        stages = []
+        for i, entry in enumerate(self.layers):
+            st = _native.ChainStage()
+            st.x = (self.hbuf[0] if i == 0 else self.h_t).data_ptr()
+            st.k, st.nseg, st.gather_seg = shape.hidden, 6, 5
+            for j, name in enumerate(("q", "k", "v", "o", "gate", "up")):
+                w, rows, _ = entry[name]
+                st.w[j], st.n[j] = w.data_ptr(), rows[1] - rows[0]
+                if name != "up":
+                    st.out[j] = self.a_out[name][:, rows[0]:].data_ptr()
+            r0 = entry["up"][1][0]
+            for q in range(world):
+                st.peer_out[q] = bases["upt"][q] + r0 * 4
+            stages.append(st)
+            st = _native.ChainStage()
+            w, rows, _ = entry["down"]
+            st.x, st.k, st.nseg, st.gather_seg = self.up_t.data_ptr(), shape.ffn, 1, 0
+            st.w[0], st.n[0] = w.data_ptr(), rows[1] - rows[0]
+            for q in range(world):
+                st.peer_out[q] = bases["ht"][q] + rows[0] * 4
+            stages.append(st)
+        sync = _native.ChainSync()
+        sync.npeers, sync.rank = world, rank
+        sync.epoch = self.epoch.data_ptr()
+        sync.final_in, sync.final_out = self.h_t.data_ptr(), self.out.data_ptr()
+        with torch.cuda.device(self.device):
+            self._plan = _native.chain_create(stages, sync)
+
+    def trace_step(self, x):
+        """Run one eager step of the persistent kernel with its timeline on and
+        return it as an int64 tensor [stages, CTAs, slots] of global-timer ns
+        (slots: entered, flags seen, x staged, warps done, flag published, then
+        each warp's last item)."""
+        if not self.persistent:
+            raise ValueError("trace_step needs persistent=True")
+        grid, slots = _native.chain_info(self._plan)
+        buf = torch.zeros((2 * self.shape.layers, grid, slots), dtype=torch.int64, device=self.device)
+        _native.chain_trace(self._plan, buf)
+        try:
+            self.forward_eager(x)
+            torch.cuda.synchronize(self.device)
+        finally:
+            _native.chain_trace(self._plan, None)
+        return buf.cpu()
+
+    def _ipc_region(self, sizes):
+        """One zeroed IPC allocation per rank holding the named regions (bytes,
+        each 256-byte aligned), mapped by every peer; handles are exchanged with
+        all_gather_object. Returns (uint8 tensor over it, offsets)."""
+        import torch.distributed as dist
+
+        offsets, total = {}, 0
+        for name, nbytes in sizes.items():
+            offsets[name] = total
+            total += (nbytes + 255) // 256 * 256
+        with torch.cuda.device(self.device):
+            base, handle = _native.ipc_malloc(total)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=self.group)
+        peers = []
+        with torch.cuda.device(self.device):
+            for q in range(self.world):
+                peers.append(base if q == self.rank else _native.ipc_open(handles[q]))
+        self._ipc = {"base": base, "peers": peers, "offsets": offsets}
+        self._raw = torch.as_tensor(_DeviceBytes(base, total), device=self.device)
+        return self._raw, offsets
+
+    def _setup_p2p(self):
+        """Launch-per-stage gathers: regions [hbuf0][hbuf1][up_full][flags]."""
+        shape, m, world = self.shape, self.shape.tokens, self.world
+        self._slots = 2 * shape.layers
+        raw, offsets = self._ipc_region({"h0": m * shape.hidden * 2, "h1": m * shape.hidden * 2,
+                                         "up": m * shape.ffn * 2, "flags": self._slots * world * 4})
+        view = lambda off, n: raw[off:off + n * 2].view(torch.bfloat16).view(m, n // m)  # noqa: E731
+        self.hbuf = [view(offsets["h0"], m * shape.hidden), view(offsets["h1"], m * shape.hidden)]
+        self.up_full = view(offsets["up"], m * shape.ffn)
+        self.flags = raw[offsets["flags"]:offsets["flags"] + self._slots * world * 4].view(torch.int32)
+        # epoch (word 0) and the CTA completion counter (word 32) on separate lines.
+        self.ctrl = torch.zeros(64, dtype=torch.int32, device=self.device)
+        self.epoch, self.done = self.ctrl[0:1], self.ctrl[32:33]
+        self._gathers = self._make_gathers()
+
+    def _make_gathers(self):
+        """The Gather descriptors of every launch of a step (they never change)."""
+        ipc, world, rank = self._ipc, self.world, self.rank
+        off = ipc["offsets"]
+        flags = [a + off["flags"] for a in ipc["peers"]]
+        local_flags = ipc["base"] + off["flags"]
+        epoch, done = self.epoch.data_ptr(), self.done.data_ptr()
+        gathers = []
+        for kind, i, wait_slot, signal_slot in p2p_schedule(self.shape.layers):
+            if kind == "end":
+                break
+            entry = self.layers[i]
+            if kind == "stage_a":
+                r0 = entry["up"][1][0]
+                dst, seg = off["up"], 5
+            else:
+                r0 = entry["down"][1][0]
+                dst, seg = off["h1" if i % 2 == 0 else "h0"], 0
+            gathers.append(_native.make_gather(
+                world, rank, epoch, seg=seg, peer_out=[a + dst + r0 * 2 for a in ipc["peers"]],
+                peer_flags=flags, signal_slot=signal_slot, wait_flags=local_flags if wait_slot >= 0 else None,
+                wait_slot=wait_slot, done=done))
+        return gathers
 
     def weight_bytes(self):
         return sum(w.numel() * 2 for layer in self.layers for (w, _, _) in layer.values())
 
     def launches_per_step(self):
-        return (2 if self.fuse else 7) * self.shape.layers
+        """Kernels of this library per step (p2p adds the epoch and end-wait kernels)."""
+        if self.persistent:
+            return 1
+        return (2 if self.fuse else 7) * self.shape.layers + (2 if self.gather == "p2p" else 0)
 
     def _proj(self, x, w, rows, n, out, k):
         """Rows [r0, r1) of this projection into columns [r0, r1) of the full-width `out`."""
@@ -147,9 +333,38 @@ class ProjectionChain:
             dist.all_gather_into_tensor(tmp.view(-1), chunk.view(-1), group=self.group)
             full.copy_(tmp.permute(1, 0, 2).reshape(m, n))
 
+    def _forward_p2p(self, x):
+        shape, world = self.shape, self.world
+        stream = torch.cuda.current_stream(self.device)
+        _native.step_begin(self.epoch, stream)
+        self.hbuf[0].copy_(x)
+        for i, entry in enumerate(self.layers):
+            h, nxt = self.hbuf[i % 2], self.hbuf[(i + 1) % 2]
+            outs = dict(self.a_out, up=self.up_full)
+            segments = []
+            for name in ("q", "k", "v", "o", "gate", "up"):
+                w, rows, n = entry[name]
+                out = outs[name]
+                segments.append((w, None, out[:, rows[0]:], out.shape[1], rows[1] - rows[0]))
+            _native.gemv_multi(_native.W_BF16, _native.DT_BF16, h, segments, None, _native.DT_BF16, h.shape[0],
+                               shape.hidden, gather=self._gathers[2 * i])
+            w, rows, _ = entry["down"]
+            _native.gemv_multi(_native.W_BF16, _native.DT_BF16, self.up_full,
+                               [(w, None, nxt[:, rows[0]:], shape.hidden, rows[1] - rows[0])], None,
+                               _native.DT_BF16, h.shape[0], shape.ffn, gather=self._gathers[2 * i + 1])
+        _native.wait_flags(self._ipc["base"] + self._ipc["offsets"]["flags"], 2 * shape.layers - 1, world,
+                           self.epoch, stream)
+        return self.hbuf[len(self.layers) % 2]
+
     def forward_eager(self, x):
         """One token step: h <- x, run every layer, return the final h (full width)."""
         shape = self.shape
+        if self.persistent:
+            self.hbuf[0].copy_(x)
+            _native.chain_launch(self._plan, torch.cuda.current_stream(self.device))
+            return self.out
+        if self.gather == "p2p":
+            return self._forward_p2p(x)
         self.hbuf[0].copy_(x)
         for i, entry in enumerate(self.layers):
             h, nxt = self.hbuf[i % 2], self.hbuf[(i + 1) % 2]
@@ -177,6 +392,12 @@ class ProjectionChain:
         Warm-up and capture use the chain's own stream, so split-K workspaces
         exist before capture."""
         self.static_x = x
+        if self.gather == "p2p" and self._ipc is not None:
+            import torch.distributed as dist
+
+            # Start the ranks' first gathered step together: a flag wait is bounded.
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
         self.stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self.stream):
             self.forward_eager(self.static_x)
@@ -192,5 +413,26 @@ class ProjectionChain:
         return self.out
 
     def release(self):
-        """Drop the graph (release graphs holding NCCL calls before destroying the group)."""
+        """Drop the graph (release graphs holding NCCL calls before destroying the
+        group) and, in p2p mode, unmap the peers' buffers and free this rank's
+        (collective: every rank calls it)."""
         self.graph = None
+        if self._plan is not None:
+            torch.cuda.synchronize(self.device)
+            _native.chain_destroy(self._plan)
+            self._plan = None
+        if self._ipc is None:
+            return
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)          # no rank still writes into a peer
+        with torch.cuda.device(self.device):
+            for q, a in enumerate(self._ipc["peers"]):
+                if q != self.rank:
+                    _native.ipc_close(a)
+        dist.barrier(group=self.group)          # every peer unmapped this rank's buffer
+        self.hbuf = self.up_full = self.flags = self._raw = self.h_t = self.up_t = None
+        with torch.cuda.device(self.device):
+            _native.ipc_free(self._ipc["base"])
+        self._ipc = None

@@ -64,6 +64,15 @@ int current_device_info(DeviceInfo** out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+}  // namespace
+
+int* device_status_address() {
+  DeviceInfo* info = nullptr;
+  return current_device_info(&info) == 0 ? info->status : nullptr;
+}
+
+namespace {
+
 int dtype_bytes(int dt) { return dt == KLAB_DT_F32 ? 4 : 2; }
 
 int vals_of(int wfmt) {
@@ -168,7 +177,8 @@ size_t workspace_need(int tiles, int mt, int n, int chunks) {
 
 int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const void* const* w,
                    const void* const* aux, const float* gscale, void* const* out, const int* ldo, const int* nrows,
-                   int out_dt, int m, int k, void* ws, size_t ws_bytes, void* stream) {
+                   int out_dt, int m, int k, void* ws, size_t ws_bytes, void* stream,
+                   const klab_gather_t* gather = nullptr) {
   if (!x || !w || !out || !ldo || !nrows || nseg < 1 || nseg > kMaxSegs) return KLAB_E_INVALID;
   if (m <= 0 || k <= 0 || ldx < k) return KLAB_E_INVALID;
   if (wfmt < W_BF16 || wfmt > W_FP4_G16E) return KLAB_E_UNSUPPORTED;
@@ -199,6 +209,17 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   const bool x_global_ok =
       aligned16(x) && (static_cast<long long>(ldx) * xb) % 16 == 0 && k % vals == 0;
 
+  if (gather && gather->npeers > 0) {
+    if (gather->npeers > kMaxPeers || gather->rank < 0 || gather->rank >= gather->npeers || !gather->epoch)
+      return KLAB_E_INVALID;
+    if (gather->seg >= nseg || (gather->seg >= 0 && out_dt != KLAB_DT_BF16)) return KLAB_E_UNSUPPORTED;
+    if (gather->signal_slot >= 0 && !gather->done) return KLAB_E_INVALID;
+    for (int q = 0; q < gather->npeers; ++q) {
+      if (gather->seg >= 0 && !gather->peer_out[q]) return KLAB_E_INVALID;
+      if (gather->signal_slot >= 0 && !gather->peer_flags[q]) return KLAB_E_INVALID;
+    }
+  }
+  const bool gathered_x = gather && gather->npeers > 0 && gather->wait_flags;
   int mt = tile_for(m);
   int xmode = XM_SMEM;
   const bool x16 = KLAB_PREFER_X16 && (wfmt == W_BF16 || wfmt == W_F16 || wfmt == W_CBF16) && xdt != KLAB_DT_F32;
@@ -211,7 +232,8 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
       xmode = XM_SMEM;
       break;
     }
-    if (x_global_ok) {
+    // Gathered x must be staged (its global reads bypass L1); never read it in place.
+    if (x_global_ok && !gathered_x) {
       xmode = XM_GLOBAL;
       break;
     }
@@ -241,6 +263,23 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   p.x = x;
   p.gscale = gscale;
   p.nseg = nseg;
+  p.gather.seg = -1;
+  p.gather.signal_slot = -1;
+  p.gather.wait_slot = -1;
+  if (gather && gather->npeers > 0) {
+    p.gather.npeers = gather->npeers;
+    p.gather.rank = gather->rank;
+    p.gather.seg = gather->seg;
+    for (int q = 0; q < gather->npeers; ++q) {
+      p.gather.peer_out[q] = gather->peer_out[q];
+      p.gather.peer_flags[q] = gather->peer_flags[q];
+    }
+    p.gather.signal_slot = gather->signal_slot;
+    p.gather.wait_flags = gather->wait_flags;
+    p.gather.wait_slot = gather->wait_slot;
+    p.gather.epoch = gather->epoch;
+    p.gather.done = gather->done;
+  }
   bool tma = g_opt_generic.load() == 0;
   int row0 = 0;
   for (int i = 0; i < nseg; ++i) {
@@ -362,6 +401,14 @@ int klab_gemv_multi(int wfmt, int xdtype, const void* x, int ldx, int nseg, cons
                     int out_dtype, int m, int k, void* workspace, size_t workspace_bytes, void* stream) {
   return run_gemv_multi(wfmt, xdtype, x, ldx, nseg, w, aux, gscale, out, ldo, n, out_dtype, m, k, workspace,
                         workspace_bytes, stream);
+}
+
+int klab_gemv_multi_gather(int wfmt, int xdtype, const void* x, int ldx, int nseg, const void* const* w,
+                           const void* const* aux, const float* gscale, void* const* out, const int* ldo,
+                           const int* n, int out_dtype, int m, int k, const klab_gather_t* gather, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  return run_gemv_multi(wfmt, xdtype, x, ldx, nseg, w, aux, gscale, out, ldo, n, out_dtype, m, k, workspace,
+                        workspace_bytes, stream, gather);
 }
 
 size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k) {

@@ -1,0 +1,574 @@
+// Persistent projection chain: one launch runs every projection of a token step.
+//
+// The chain (BF16 weights, one token) is a list of stages; stage s > 0 reads the
+// gathered output of stage s-1. One CTA per SM (cooperative launch), 16 warps,
+// each with a private ring of kChainDepth bulk-copy slots (one slot = one row x
+// 4 KiB chunk of weights = one "item").
+//
+// Work: each stage's n*S items are dealt to the warps as contiguous runs of
+// equal length (no atomics). A warp's lane 0 issues its next item as soon as a
+// slot is consumed, running on into the next stage's run, so the weight stream
+// of stage s+1 is in flight while the stage-s data dependency is still being
+// resolved (weights never depend on activations). Rows inside one run are
+// folded in registers. A row cut by a run boundary publishes tagged per-chunk
+// partials (64-bit words: tag << 32 | fp32 bits); the warp whose run holds the
+// row's last chunk folds them after the rest of its run, polling for the tags
+// (at most one such row per warp and stage), so no warp ever waits in the
+// middle of its run and no tickets, atomics or fences are needed.
+//
+// Data exchange: the outputs that later stages read (the gathered segment of a
+// stage) are written as 32-bit words (tag << 16 | bf16) into every rank's copy
+// of the gather buffer, over NVLink for the peers; the tag identifies the step
+// and stage. A CTA stages x for stage s by polling those words until every one
+// carries stage s-1's tag (bounded by time). No grid barrier, no counters and no
+// system-scope fence sit between stages: each 32-bit store is single-copy
+// atomic, so a word with the right tag holds the right value. A CTA that holds
+// no unit of a stage skips staging that stage's x (it may already be
+// overwritten by later stages, whose producers only wait for CTAs that hold
+// units).
+//
+// Arithmetic order is the one of stream_gemv_kernel (a function of K only):
+// chunk partials by the same per-lane tree and warp butterfly, row total folded
+// over chunks in order, one RNE to BF16.
+// The chain's outputs are therefore bit-identical to one launch per stage.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "klab_kernels.h"
+#include "stream_gemv.cuh"
+
+namespace klab {
+namespace {
+
+constexpr int kChainWarps = 16;
+constexpr int kChainDepth = 3;
+constexpr int kChainKC = Layout<W_BF16>::KC;  // 2048 columns per item
+constexpr int kChainSlot = kWeightSlot;       // 4096 bytes per item
+constexpr int kChainMaxK = 16384;             // x staging capacity (BF16 values)
+constexpr int kChainMaxS = kChainMaxK / kChainKC;
+constexpr int kChainBarBytes = 512;           // mbarriers
+constexpr int kChainSmem = kChainBarBytes + kChainWarps * kChainDepth * kChainSlot + kChainMaxK * 2;
+constexpr int kChainMaxStages = 4096;
+constexpr unsigned long long kChainWaitNs = 2000000000ull;  // polling limit per stage (2 s)
+
+struct ChainSeg {
+  const char* w;  // BF16 [rows, k]
+  void* out;      // BF16 outputs (plain segments)
+  int row0;       // first stage row of this segment
+  int pad;
+};
+
+struct ChainStage {
+  const void* x;         // stage 0: BF16 [k]; later stages: tagged words [k]
+  int k, chunks, n, nseg;
+  long long ws_off;      // this stage's tagged partials [n][S] (64-bit words)
+  int gather_seg;        // segment written as tagged words to every rank
+  int pad;
+  ChainSeg seg[kMaxSegs];
+  unsigned* peer_out[kMaxPeers];  // rank q's tagged buffer, at gather_seg's first row
+};
+
+struct ChainParams {
+  const ChainStage* stages;
+  int nstages;
+  int npeers, rank;
+  unsigned* epoch;                 // completed steps (this rank)
+  unsigned* exits;                 // CTAs finished with the step, zero between steps
+  unsigned long long* ws;          // tagged split-row partials
+  int* status;
+  const unsigned* final_in;        // tagged output of the last stage
+  unsigned short* final_out;       // its BF16 values
+  int final_n;
+  unsigned long long* trace;       // optional: [nstages][grid][kTraceSlots] global-timer ns
+};
+
+// Trace slots per (stage, CTA): entered, x staged, then each warp's last item.
+constexpr int kTraceCta = 2;
+constexpr int kTraceSlots = kTraceCta + kChainWarps;
+
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void trace_mark(const ChainParams& p, int s, int slot) {
+  if (p.trace) p.trace[(static_cast<long long>(s) * gridDim.x + blockIdx.x) * kTraceSlots + slot] = global_ns();
+}
+
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Tag of stage s's outputs in step `epoch` (never 0, the value of a fresh buffer).
+__device__ __forceinline__ unsigned stage_tag(unsigned epoch, int nstages, int s) {
+  return 1u + (epoch * static_cast<unsigned>(nstages) + static_cast<unsigned>(s)) % 65535u;
+}
+
+__device__ __forceinline__ int seg_of(const ChainStage& st, int row) {
+  int s = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxSegs; ++i)
+    if (i < st.nseg && row >= st.seg[i].row0) s = i;
+  return s;
+}
+
+// This warp's contiguous run [begin, end) of a stage's n*S items.
+__device__ __forceinline__ void warp_range(const ChainStage& st, unsigned gw, unsigned nw, long long* begin,
+                                           long long* end) {
+  const long long T = static_cast<long long>(st.n) * st.chunks;
+  *begin = T * gw / nw;
+  *end = T * (gw + 1) / nw;
+}
+
+// Issue side of one warp's item sequence over all stages (lane 0 only).
+struct IssueCursor {
+  int stage, row, c;
+  long long left;  // items left in this stage's run
+  __device__ __forceinline__ void enter(const ChainParams& p, unsigned gw, unsigned nw, int s) {
+    for (stage = s; stage < p.nstages; ++stage) {
+      long long b, e;
+      warp_range(p.stages[stage], gw, nw, &b, &e);
+      if (e > b) {
+        const int S = p.stages[stage].chunks;
+        row = static_cast<int>(b / S);
+        c = static_cast<int>(b - static_cast<long long>(row) * S);
+        left = e - b;
+        return;
+      }
+    }
+  }
+  __device__ __forceinline__ bool valid(const ChainParams& p) const { return stage < p.nstages; }
+  // Issue the current item into `slot`, then advance.
+  __device__ __forceinline__ void issue(const ChainParams& p, unsigned gw, unsigned nw, unsigned slot,
+                                        unsigned bar) {
+    const ChainStage& st = p.stages[stage];
+    const int s = seg_of(st, row);
+    const int L = min(kChainKC, st.k - c * kChainKC);
+    const char* src = st.seg[s].w + (static_cast<long long>(row - st.seg[s].row0) * st.k + c * kChainKC) * 2;
+    fence_proxy_async_smem();
+    mbar_arrive_expect_tx(bar, L * 2);
+    bulk_g2s(slot, src, L * 2, bar);
+    if (--left == 0) {
+      enter(p, gw, nw, stage + 1);
+    } else if (++c == st.chunks) {
+      c = 0;
+      ++row;
+    }
+  }
+};
+
+__device__ __forceinline__ void chain_finalize(const ChainParams& p, const ChainStage& st, int row, float v,
+                                               unsigned tag) {
+  const int s = seg_of(st, row);
+  const int local = row - st.seg[s].row0;
+  const unsigned short b = f32_to_bf16_rn(v);
+  if (s == st.gather_seg) {
+    const unsigned word = (tag << 16) | b;
+    for (int q = 0; q < p.npeers; ++q) st_relaxed_sys(st.peer_out[q] + local, word);
+  } else {
+    static_cast<unsigned short*>(st.seg[s].out)[local] = b;
+  }
+}
+
+// Stage x into shared memory as BF16 (natural order, zero-padded to whole
+// 256-column segments). Tagged inputs are polled until every word carries
+// `tag`; returns false when the time limit passed first.
+__device__ bool stage_chain_x(const ChainStage& st, bool tagged, unsigned tag, unsigned char* xs, int* broken) {
+  const int k = st.k;
+  const int segs = (k + 255) / 256;
+  bool ok = true;
+  if (!tagged) {
+    const uint4* src = static_cast<const uint4*>(st.x);
+    for (int u = threadIdx.x; u < segs * 32; u += blockDim.x) {
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (u * 8 < k) v = __ldcg(src + u);
+      reinterpret_cast<uint4*>(xs)[u] = v;
+    }
+    return true;
+  }
+  // Four tagged words (16 bytes) -> four BF16 values (8 bytes) per vector.
+  // All of a thread's vectors are loaded at once; only stale ones are re-read.
+  const char* src = static_cast<const char*>(st.x);
+  constexpr int kPer = kChainMaxK / 4 / (kChainWarps * 32);  // vectors per thread at most
+  const int nvec = segs * 64;
+  uint4 v[kPer];
+  bool fresh[kPer];
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int u = threadIdx.x + j * blockDim.x;
+    fresh[j] = true;
+    v[j] = make_uint4(0u, 0u, 0u, 0u);
+    if (u < nvec && u * 4 < k) v[j] = ld_volatile_v4(src + 16ll * u);
+  }
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    bool all = true;
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int u = threadIdx.x + j * blockDim.x;
+      if (u < nvec && u * 4 < k) {
+        fresh[j] = (v[j].x >> 16) == tag && (v[j].y >> 16) == tag && (v[j].z >> 16) == tag && (v[j].w >> 16) == tag;
+        all = all && fresh[j];
+      }
+    }
+    if (all) break;
+    if (*reinterpret_cast<volatile int*>(broken) || global_ns() - t0 > kChainWaitNs) {
+      ok = false;
+      *reinterpret_cast<volatile int*>(broken) = 1;
+      break;
+    }
+    __nanosleep(32);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int u = threadIdx.x + j * blockDim.x;
+      if (!fresh[j]) v[j] = ld_volatile_v4(src + 16ll * u);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < kPer; ++j) {
+    const int u = threadIdx.x + j * blockDim.x;
+    if (u < nvec)
+      reinterpret_cast<uint2*>(xs)[u] =
+          make_uint2((v[j].x & 0xffffu) | (v[j].y << 16), (v[j].z & 0xffffu) | (v[j].w << 16));
+  }
+  return ok;
+}
+
+// Fold of a split row: poll its S tagged partials (bounded by time), add them
+// in chunk order and finalize. Lane 0 only.
+__device__ __forceinline__ void fold_split_row(const ChainParams& p, const ChainStage& st, int row, unsigned tag,
+                                               int* broken) {
+  const int S = st.chunks;
+  const unsigned long long* part = p.ws + st.ws_off + static_cast<long long>(row) * S;
+  unsigned long long w[kChainMaxS];
+#pragma unroll
+  for (int cc = 0; cc < kChainMaxS; ++cc) w[cc] = cc < S ? ld_relaxed_gpu_u64(part + cc) : 0ull;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    bool all = true;
+#pragma unroll
+    for (int cc = 0; cc < kChainMaxS; ++cc)
+      if (cc < S && static_cast<unsigned>(w[cc] >> 32) != tag) all = false;
+    if (all) break;
+    if (*reinterpret_cast<volatile int*>(broken) || global_ns() - t0 > kChainWaitNs) {
+      *reinterpret_cast<volatile int*>(broken) = 1;
+      record_status(p.status, kStatusFlagTimeout);
+      break;
+    }
+    __nanosleep(32);
+#pragma unroll
+    for (int cc = 0; cc < kChainMaxS; ++cc)
+      if (cc < S && static_cast<unsigned>(w[cc] >> 32) != tag) w[cc] = ld_relaxed_gpu_u64(part + cc);
+  }
+  float v[kChainMaxS];
+#pragma unroll
+  for (int cc = 0; cc < kChainMaxS; ++cc) v[cc] = __uint_as_float(static_cast<unsigned>(w[cc]));
+  float total = v[0];
+#pragma unroll
+  for (int cc = 1; cc < kChainMaxS; ++cc)
+    if (cc < S) total = add_rn(total, v[cc]);
+  chain_finalize(p, st, row, total, tag);
+}
+
+__global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ int s_broken;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const unsigned gw = blockIdx.x * kChainWarps + warp, nw = gridDim.x * kChainWarps;
+  const unsigned pbar0 = smem_addr(smem) + warp * kChainDepth * 8;
+  const unsigned slot0 = smem_addr(smem) + kChainBarBytes + warp * kChainDepth * kChainSlot;
+  unsigned char* xs = smem + kChainBarBytes + kChainWarps * kChainDepth * kChainSlot;
+  const unsigned xs_lane0 = smem_addr(xs) + lane * 16;
+  if (threadIdx.x == 0) s_broken = 0;
+
+  // Ring prologue: the first kChainDepth items of this warp's sequence.
+  IssueCursor iss{};
+  long long issued = 0;  // lane 0: items issued so far
+  if (lane == 0) {
+    for (int i = 0; i < kChainDepth; ++i) mbar_init(pbar0 + 8 * i, 1);
+    fence_mbar_init();
+    iss.enter(p, gw, nw, 0);
+    for (int i = 0; i < kChainDepth && iss.valid(p); ++i) {
+      iss.issue(p, gw, nw, slot0 + i * kChainSlot, pbar0 + i * 8);
+      ++issued;
+    }
+  }
+  __syncwarp();
+
+  const unsigned epoch = *p.epoch + 1u;  // this step
+  bool ok = true;
+  long long g = 0;        // ring position of the next item to consume
+  long long failed = -1;  // ring position of a copy that never completed
+
+  for (int s = 0; s < p.nstages; ++s) {
+    const ChainStage& st = p.stages[s];
+    const int S = st.chunks, k = st.k;
+    long long wbegin, wend;
+    warp_range(st, gw, nw, &wbegin, &wend);
+    const int nitems = static_cast<int>(wend - wbegin);
+    if (threadIdx.x == 0) trace_mark(p, s, 0);
+    // Barrier (every warp is done with the previous x); stage x if any warp
+    // of this CTA has items in this stage.
+    if (__syncthreads_or(nitems > 0 ? 1 : 0)) {
+      const bool tagged = s > 0;
+      if (!stage_chain_x(st, tagged, tagged ? stage_tag(epoch, p.nstages, s - 1) : 0u, xs, &s_broken))
+        record_status(p.status, kStatusFlagTimeout);
+      __syncthreads();
+    }
+    if (threadIdx.x == 0) trace_mark(p, s, 1);
+    const unsigned tag = stage_tag(epoch, p.nstages, s);
+
+    int row = 0, c = 0;
+    if (nitems > 0) {
+      row = static_cast<int>(wbegin / S);
+      c = static_cast<int>(wbegin - static_cast<long long>(row) * S);
+    }
+    // The row cut by this run's start whose last chunk lies in this run is
+    // folded after the run (its earlier chunks come from preceding warps).
+    int deferred = -1;
+    float rowsum = 0.0f;
+    bool whole = true;
+    for (int q = 0; q < nitems; ++q, ++g) {
+      const int L = min(kChainKC, k - c * kChainKC);
+      const unsigned slot = slot0 + static_cast<unsigned>(g % kChainDepth) * kChainSlot;
+      const unsigned bar = pbar0 + static_cast<unsigned>(g % kChainDepth) * 8;
+      float P[1] = {0.0f};
+      if (ok) {
+        const bool landed = mbar_wait(bar, static_cast<unsigned>((g / kChainDepth) & 1));
+        ok = __all_sync(0xffffffffu, landed);
+        if (!ok) failed = g;
+      }
+      if (ok) {
+        const unsigned xs_lane = xs_lane0 + c * kSegs * 512;
+        if (L == kChainKC)
+          compute_item<W_BF16, X_BF16, XM_SMEM16, 1, true>(slot, 0, 0, lane, L, xs_lane, 0, nullptr, 0, 1, P);
+        else
+          compute_item<W_BF16, X_BF16, XM_SMEM16, 1, false>(slot, 0, 0, lane, L, xs_lane, 0, nullptr, 0, 1, P);
+        __syncwarp();  // every lane is done with the slot before it is refilled
+        if (lane == 0 && iss.valid(p)) {
+          iss.issue(p, gw, nw, slot, bar);
+          ++issued;
+        }
+      }
+      if (c == 0 || q == 0)
+        whole = static_cast<long long>(row) * S >= wbegin && static_cast<long long>(row) * S + S <= wend;
+      if (whole) {
+        rowsum = (c == 0) ? P[0] : add_rn(rowsum, P[0]);
+        if (c == S - 1 && lane == 0) chain_finalize(p, st, row, rowsum, tag);
+      } else {
+        if (lane == 0)
+          st_relaxed_gpu_u64(p.ws + st.ws_off + static_cast<long long>(row) * S + c,
+                             (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(P[0]));
+        if (c == S - 1) deferred = row;
+      }
+      if (++c == S) {
+        c = 0;
+        ++row;
+      }
+    }
+    if (deferred >= 0 && lane == 0) fold_split_row(p, st, deferred, tag, &s_broken);
+    if (lane == 0) trace_mark(p, s, kTraceCta + warp);
+  }
+
+  // CTA 0 publishes the step's output once every rank's last-stage words are in.
+  if (blockIdx.x == 0) {
+    const unsigned tag = stage_tag(epoch, p.nstages, p.nstages - 1);
+    const unsigned long long t0 = global_ns();
+    for (int j = threadIdx.x; j < p.final_n; j += blockDim.x) {
+      unsigned v = 0;
+      for (;;) {
+        asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p.final_in + j) : "memory");
+        if ((v >> 16) == tag) break;
+        if (*reinterpret_cast<volatile int*>(&s_broken) || global_ns() - t0 > kChainWaitNs) {
+          *reinterpret_cast<volatile int*>(&s_broken) = 1;
+          record_status(p.status, kStatusFlagTimeout);
+          break;
+        }
+        __nanosleep(32);
+      }
+      p.final_out[j] = static_cast<unsigned short>(v & 0xffffu);
+    }
+  }
+
+  if (!ok) {
+    record_status(p.status, kStatusMbarTimeout);
+    // Drain copies still in flight (bounded) before shared memory is released.
+    if (lane == 0)
+      for (long long i = failed; i < issued; ++i)
+        mbar_wait(pbar0 + static_cast<unsigned>(i % kChainDepth) * 8, static_cast<unsigned>((i / kChainDepth) & 1));
+  }
+
+  // The last CTA to finish advances the step (every CTA read it at its start).
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(p.exits, 1u) == gridDim.x - 1) {
+    *p.exits = 0u;
+    *p.epoch = epoch;
+  }
+}
+
+struct ChainPlan {
+  ChainParams params{};
+  ChainStage* d_stages = nullptr;
+  void* d_ws = nullptr;
+  int grid = 0;
+};
+
+}  // namespace
+}  // namespace klab
+
+using klab::ChainPlan;
+
+extern "C" {
+
+KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, const klab_chain_sync_t* sync,
+                               void** plan_out) {
+  using namespace klab;
+  if (!stages || !sync || !plan_out || nstages <= 0 || nstages > kChainMaxStages) return KLAB_E_INVALID;
+  if (sync->npeers < 1 || sync->npeers > kMaxPeers || sync->rank < 0 || sync->rank >= sync->npeers ||
+      !sync->epoch || !sync->final_out)
+    return KLAB_E_INVALID;
+  if (!sync->final_in || (reinterpret_cast<uintptr_t>(sync->final_in) & 3)) return KLAB_E_INVALID;
+  std::vector<ChainStage> host(nstages);
+  long long ws_words = 0;
+  for (int s = 0; s < nstages; ++s) {
+    const klab_chain_stage_t& in = stages[s];
+    ChainStage& st = host[s];
+    std::memset(&st, 0, sizeof(st));
+    if (!in.x || in.k <= 0 || in.k > kChainMaxK || in.k % 8 || in.nseg < 1 || in.nseg > kMaxSegs)
+      return KLAB_E_SHAPE;
+    if (reinterpret_cast<uintptr_t>(in.x) & 15) return KLAB_E_ALIGN;
+    // Every stage feeds the next (or the step output) through its gathered segment.
+    if (in.gather_seg < 0 || in.gather_seg >= in.nseg) return KLAB_E_INVALID;
+    if (s > 0 && in.k != stages[s - 1].n[stages[s - 1].gather_seg] * sync->npeers) return KLAB_E_SHAPE;
+    st.x = in.x;
+    st.k = in.k;
+    st.chunks = (in.k + kChainKC - 1) / kChainKC;
+    st.nseg = in.nseg;
+    st.gather_seg = in.gather_seg;
+    int rows = 0;
+    for (int i = 0; i < in.nseg; ++i) {
+      if (!in.w[i] || in.n[i] <= 0 || (i != in.gather_seg && !in.out[i])) return KLAB_E_INVALID;
+      if (reinterpret_cast<uintptr_t>(in.w[i]) & 15) return KLAB_E_ALIGN;
+      st.seg[i].w = static_cast<const char*>(in.w[i]);
+      st.seg[i].out = in.out[i];
+      st.seg[i].row0 = rows;
+      rows += in.n[i];
+    }
+    for (int q = 0; q < sync->npeers; ++q) {
+      if (!in.peer_out[q] || (reinterpret_cast<uintptr_t>(in.peer_out[q]) & 3)) return KLAB_E_INVALID;
+      st.peer_out[q] = static_cast<unsigned*>(in.peer_out[q]);
+    }
+    st.n = rows;
+    st.ws_off = ws_words;
+    ws_words += static_cast<long long>(rows) * st.chunks;
+  }
+
+  int dev = 0, sms = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (err != cudaSuccess) return err;
+  err = cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kChainSmem);
+  if (err != cudaSuccess) return err;
+  int per_sm = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kChainWarps * 32, kChainSmem);
+  if (err != cudaSuccess) return err;
+  if (per_sm < 1) return KLAB_E_UNSUPPORTED;
+
+  ChainPlan* plan = new ChainPlan();
+  plan->grid = sms;
+  const size_t stage_bytes = sizeof(ChainStage) * nstages;
+  // [exit count][tagged partials]; partials never need clearing (tags).
+  const size_t total = 256 + static_cast<size_t>(ws_words) * 8;
+  err = cudaMalloc(reinterpret_cast<void**>(&plan->d_stages), stage_bytes);
+  if (err == cudaSuccess) err = cudaMemcpy(plan->d_stages, host.data(), stage_bytes, cudaMemcpyHostToDevice);
+  if (err == cudaSuccess) err = cudaMalloc(&plan->d_ws, total);
+  if (err == cudaSuccess) err = cudaMemset(plan->d_ws, 0, total);
+  if (err != cudaSuccess) {
+    cudaFree(plan->d_stages);
+    cudaFree(plan->d_ws);
+    delete plan;
+    return err;
+  }
+  ChainParams& p = plan->params;
+  char* base = static_cast<char*>(plan->d_ws);
+  p.stages = plan->d_stages;
+  p.nstages = nstages;
+  p.npeers = sync->npeers;
+  p.rank = sync->rank;
+  p.epoch = sync->epoch;
+  p.exits = reinterpret_cast<unsigned*>(base);
+  p.ws = reinterpret_cast<unsigned long long*>(base + 256);
+  p.status = device_status_address();
+  p.final_in = sync->final_in;
+  p.final_out = static_cast<unsigned short*>(sync->final_out);
+  p.final_n = stages[nstages - 1].n[stages[nstages - 1].gather_seg] * sync->npeers;
+  *plan_out = plan;
+  return 0;
+}
+
+KLAB_API int klab_chain_info(void* plan_ptr, int* grid, int* trace_slots) {
+  using namespace klab;
+  ChainPlan* plan = static_cast<ChainPlan*>(plan_ptr);
+  if (!plan) return KLAB_E_INVALID;
+  if (grid) *grid = plan->grid;
+  if (trace_slots) *trace_slots = kTraceSlots;
+  return 0;
+}
+
+KLAB_API int klab_chain_trace(void* plan_ptr, unsigned long long* buffer, size_t bytes) {
+  using namespace klab;
+  ChainPlan* plan = static_cast<ChainPlan*>(plan_ptr);
+  if (!plan) return KLAB_E_INVALID;
+  if (buffer && bytes < static_cast<size_t>(plan->params.nstages) * plan->grid * kTraceSlots * 8)
+    return KLAB_E_SHAPE;
+  plan->params.trace = buffer;
+  return 0;
+}
+
+KLAB_API int klab_chain_launch(void* plan_ptr, void* stream) {
+  using namespace klab;
+  ChainPlan* plan = static_cast<ChainPlan*>(plan_ptr);
+  if (!plan) return KLAB_E_INVALID;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(plan->grid);
+  cfg.blockDim = dim3(kChainWarps * 32);
+  cfg.dynamicSmemBytes = kChainSmem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, chain_kernel, plan->params);
+}
+
+KLAB_API int klab_chain_destroy(void* plan_ptr) {
+  ChainPlan* plan = static_cast<ChainPlan*>(plan_ptr);
+  if (!plan) return KLAB_E_INVALID;
+  cudaFree(plan->d_stages);
+  cudaFree(plan->d_ws);
+  delete plan;
+  return 0;
+}
+
+}  // extern "C"

@@ -69,7 +69,7 @@ __device__ __forceinline__ bool mbar_wait(unsigned bar, unsigned parity) {
 
 // ------------------------------------------------------------------ bulk copy
 
-// 1-D bulk copy global -> shared (no tensor map, no multicast). dst, src and
+// 1-D bulk copy global -> shared (no tensor map, this CTA only). dst, src and
 // bytes must be multiples of 16; completion is signalled on `bar`.
 __device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned bytes,
                                          unsigned bar) {
@@ -84,6 +84,33 @@ __device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned
 // async-proxy (bulk copy) writes to the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ peer flags
+
+// System-scope acquire load of a 32-bit flag (written by peers over NVLink).
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// System-scope acquire-release fence: orders this thread's earlier accesses, and
+// those it has observed (e.g. its CTA's stores, through a barrier), before its
+// later ones for observers on any GPU of the node.
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ void st_relaxed_sys(unsigned* p, unsigned v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *flag >= target (monotonic epochs); false on timeout.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned* flag, unsigned target) {
+  for (unsigned i = 0; i < kSpinLimit; ++i) {
+    if (static_cast<int>(ld_acquire_sys(flag) - target) >= 0) return true;
+    __nanosleep(64);
+  }
+  return false;
 }
 
 // ------------------------------------------------------------------ PDL

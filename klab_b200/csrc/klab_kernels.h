@@ -5,6 +5,8 @@
 #include "../../include/klab_b200.h"
 
 namespace klab {
+// Device address of the status word on the current device (nullptr on error).
+int* device_status_address();
 cudaError_t launch_cbf16_unpack(const void* payload, const unsigned* metadata, void* out, int n, int k,
                                 cudaStream_t stream);
 cudaError_t launch_int8_dequant(const void* codes, const float* scales, int group, float* out, int n, int k,

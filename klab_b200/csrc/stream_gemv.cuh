@@ -11,7 +11,7 @@
 //   W_FP4_G16E E2M1 + E4M3 scale per 16 + fp32 global (fp4_kernels.cu, fp4.py:33-60)
 //
 // Data movement (B200): every warp owns a private ring of DEPTH shared-memory
-// slots filled by 1-D bulk copies (cp.async.bulk, no multicast) with mbarrier
+// slots filled by 1-D bulk copies (cp.async.bulk into this CTA only) with mbarrier
 // completion; a slot holds one "item" = one row x one K-chunk of 4 KiB of weight
 // bytes plus that chunk's scales. Weights never depend on the previous kernel, so
 // the first copies are issued before griddepcontrol.wait (programmatic dependent
@@ -133,7 +133,28 @@ struct Segment {
   int row0;         // first launch row of this segment
 };
 
+// Output gather over NVLink peer memory, fused into the projection. The
+// gathered segment's output rows are also stored into every peer's copy of the
+// full-width output buffer; when the whole grid is done, the last CTA raises this
+// rank's flag in `signal_slot` of every peer with the current epoch. A launch
+// whose x is a gathered buffer first waits (bounded) until every rank's flag in
+// `wait_slot` of the local flag array reaches the epoch. Flags are monotonic.
+constexpr int kMaxPeers = 8;
+struct Gather {
+  int npeers;                     // ranks taking part (0: no gather)
+  int rank;
+  int seg;                        // segment whose output is pushed (-1: none)
+  void* peer_out[kMaxPeers];      // rank r's copy of that segment's output buffer
+  unsigned* peer_flags[kMaxPeers];  // rank r's flag array [slots][npeers]
+  int signal_slot;                // slot raised after this launch (-1: none)
+  const unsigned* wait_flags;     // local flag array (nullptr: no wait)
+  int wait_slot;
+  const unsigned* epoch;          // current step's epoch (device word)
+  unsigned* done;                 // CTA completion counter, zero between launches
+};
+
 struct GemvParams {
+  Gather gather;
   const void* x;        // [M, ldx] activations (X format)
   const float* gscale;  // W_FP4_G16E global scale (device scalar)
   Segment seg[kMaxSegs];
@@ -175,14 +196,16 @@ __device__ __forceinline__ RowRef resolve_row(const GemvParams& p, int row) {
 // bank conflicts. XM_SMEM stores FP32 (NV = VALS/4); XM_SMEM16 stores the
 // 16-bit input values unchanged (NV = VALS/8, BF16/FP16 x only). Columns >= K
 // and tokens >= M are zero.
+// x is read with L2-only loads (ld.global.cg): peers may have written it over
+// NVLink, so no line of it may come from this SM's L1.
 template <int X>
 __device__ __forceinline__ float x_value(const void* x, long long idx) {
   if constexpr (X == X_BF16) {
-    return __uint_as_float(static_cast<unsigned>(static_cast<const unsigned short*>(x)[idx]) << 16);
+    return __uint_as_float(static_cast<unsigned>(__ldcg(static_cast<const unsigned short*>(x) + idx)) << 16);
   } else if constexpr (X == X_F16) {
-    return f16_to_f32(static_cast<const unsigned short*>(x)[idx]);
+    return f16_to_f32(__ldcg(static_cast<const unsigned short*>(x) + idx));
   } else {
-    return static_cast<const float*>(x)[idx];
+    return __ldcg(static_cast<const float*>(x) + idx);
   }
 }
 
@@ -225,7 +248,7 @@ __device__ void stage_x(const GemvParams& p, int tile, unsigned char* xs, int se
       for (int e = 0; e < 8; ++e) {
         const int col = col0 + e;
         v[e] = (token < p.m && col < p.k)
-                   ? static_cast<const unsigned short*>(p.x)[static_cast<long long>(token) * p.ldx + col]
+                   ? __ldcg(static_cast<const unsigned short*>(p.x) + static_cast<long long>(token) * p.ldx + col)
                    : static_cast<unsigned short>(0);
       }
       *reinterpret_cast<uint4*>(dst) =
@@ -574,7 +597,13 @@ __device__ __forceinline__ void finalize_token(const GemvParams& p, const RowRef
   if (p.out_f32) {
     static_cast<float*>(sg.out)[idx] = v;
   } else {
-    static_cast<unsigned short*>(sg.out)[idx] = f32_to_bf16_rn(v);
+    const unsigned short b = f32_to_bf16_rn(v);
+    static_cast<unsigned short*>(sg.out)[idx] = b;
+    if (r.seg == p.gather.seg) {
+      // Fused all-gather: the same value into every other rank's copy (NVLink stores).
+      for (int q = 0; q < p.gather.npeers; ++q)
+        if (q != p.gather.rank) static_cast<unsigned short*>(p.gather.peer_out[q])[idx] = b;
+    }
   }
 }
 
@@ -700,6 +729,13 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
   }
 
   grid_dependency_wait();
+  if (p.gather.wait_flags && threadIdx.x < p.gather.npeers) {
+    // x was gathered from the peers: wait until every rank's slice has landed.
+    const unsigned target = *p.gather.epoch;
+    if (!wait_flag_geq(p.gather.wait_flags + p.gather.wait_slot * p.gather.npeers + threadIdx.x, target))
+      record_status(p.status, kStatusFlagTimeout);
+  }
+  __syncthreads();
   if constexpr (XM != XM_GLOBAL) stage_x<F, X, XM, MT>(p, tile, xs, segs);
   __syncthreads();
   grid_launch_dependents();
@@ -843,6 +879,25 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
         issue_meta(issued_meta, mcur);
         mcur.advance(S, row_step);
         ++issued_meta;
+      }
+    }
+  }
+
+  if (p.gather.signal_slot >= 0) {
+    // The CTA's peer stores reach thread 0 through the barrier; one system-scope
+    // fence per CTA orders them before its count. The CTA that completes the
+    // count fences again (acquiring the others' counts, releasing for the peers)
+    // and raises this rank's flag on every rank.
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned total = gridDim.x * gridDim.y;
+      fence_acq_rel_sys();
+      if (atomicAdd(p.gather.done, 1u) == total - 1) {
+        *p.gather.done = 0u;
+        fence_acq_rel_sys();
+        const unsigned epoch = *p.gather.epoch;
+        for (int q = 0; q < p.gather.npeers; ++q)
+          st_relaxed_sys(p.gather.peer_flags[q] + p.gather.signal_slot * p.gather.npeers + p.gather.rank, epoch);
       }
     }
   }

@@ -86,3 +86,39 @@ def test_shard_ranges_cover_rows_exactly():
         assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
     with pytest.raises(ValueError):
         _shard(100, 0, 3)
+
+
+def test_p2p_schedule_waits_only_for_slots_signalled_earlier():
+    """Every wait in a step is for a slot signalled by an earlier launch of the
+    same step, each slot is signalled once, and each gathered buffer is written
+    by peers only after every rank has finished reading it (the reader's next
+    signal precedes the writer's wait)."""
+    from klab_b200.chain import p2p_schedule
+
+    for layers in (1, 2, 5, 32):
+        sched = p2p_schedule(layers)
+        signalled = []
+        for kind, layer, wait_slot, signal_slot in sched:
+            if wait_slot >= 0:
+                assert wait_slot in signalled, (kind, layer, wait_slot)
+            if signal_slot >= 0:
+                assert signal_slot not in signalled
+                signalled.append(signal_slot)
+        assert sorted(signalled) == list(range(2 * layers))
+        assert sched[-1] == ("end", layers, 2 * layers - 1, -1)
+        # Stage A of layer i (i > 0) writes the peers' up buffer after waiting
+        # for slot 2i-1, which every rank signals after its down of layer i-1,
+        # the last reader of that buffer.
+        for kind, layer, wait_slot, _ in sched:
+            if kind == "stage_a" and layer:
+                assert wait_slot == 2 * (layer - 1) + 1
+
+
+def test_p2p_mode_argument_checks():
+    from klab_b200.chain import ChainShape, ProjectionChain
+
+    shape = ChainShape(layers=1, hidden=64, kv=32, ffn=128)
+    with pytest.raises(ValueError):
+        ProjectionChain(shape, gather="mpi", project=lambda *a: None)
+    with pytest.raises(ValueError):
+        ProjectionChain(shape, world=2, gather="p2p", project=lambda *a: None)

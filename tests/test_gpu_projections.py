@@ -452,3 +452,34 @@ def test_chain_fused_equals_unfused_and_graph():
     ref64 = og.bf16_projection64(up, host_bits(entry["down"][0]))
     report = ob.check_outputs(ref64, ob.bf16_values(got), output_dtype="bf16")
     assert report["passed"] and report["max_ulp_error"] <= 1, report
+
+
+@pytest.mark.parametrize("dims", [(3, 512, 128, 1536), (2, 1024, 256, 3584), (2, 256, 64, 512)])
+def test_persistent_chain_equals_launch_chain(native, dims):
+    """The one-launch persistent chain (stage flags as a grid barrier, split rows
+    folded in chunk order) gives the launch-per-stage chain's bits, eagerly and
+    under graph replay, every step; every stage's local outputs match too."""
+    from klab_b200.chain import ChainShape, ProjectionChain
+
+    layers, hidden, kv, ffn = dims
+    shape = ChainShape(layers=layers, hidden=hidden, kv=kv, ffn=ffn)
+    x = dev_bf16(og.normal_bf16_bits(61 + hidden, (1, hidden), 1.0))
+    ref_chain = ProjectionChain(shape, seed=4)
+    ref = ref_chain.forward_eager(x).clone()
+    ref_a = {k: v.clone() for k, v in ref_chain.a_out.items()}
+    pc = ProjectionChain(shape, seed=4, persistent=True)
+    assert pc.launches_per_step() == 1
+    for _ in range(2):
+        got = pc.forward_eager(x)
+        torch.cuda.synchronize()
+        assert same_bits(got, ref)
+    for name, t in ref_a.items():
+        assert same_bits(pc.a_out[name], t), name
+    out = pc.capture(x)
+    for _ in range(3):
+        pc.replay()
+    torch.cuda.synchronize()
+    assert same_bits(out, ref)
+    assert int(pc.epoch.item()) == 2 + 1 + 3  # eager steps, capture warm-up, replays
+    assert native.device_status() == 0
+    pc.release()
