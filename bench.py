@@ -384,8 +384,9 @@ def main(argv=None):
     parser.add_argument("--quick", action="store_true", help="fewer rounds and shapes (smoke runs)")
     parser.add_argument("--gather", choices=("nccl", "p2p"), default="p2p",
                         help="N>1: NCCL all-gathers, or gathers fused into the projections over NVLink")
-    parser.add_argument("--persistent", action=argparse.BooleanOptionalAction, default=False,
-                        help="the whole token step as one persistent kernel launch")
+    parser.add_argument("--persistent", action=argparse.BooleanOptionalAction, default=None,
+                        help="the whole token step as one persistent kernel launch "
+                             "(default: with several GPUs; one launch per stage on one GPU)")
     args = parser.parse_args(argv)
     if args.warmup < 3:
         parser.error("--warmup must be >= 3")
@@ -411,6 +412,8 @@ def main(argv=None):
     from klab_b200 import _native
     from klab_b200.chain import ChainShape, ProjectionChain
 
+    if args.persistent is None:
+        args.persistent = world > 1
     peak, peak_kind = measured_peak()
     shape = ChainShape(layers=args.layers)
     chain = ProjectionChain(shape, rank=rank, world=world, group=group, seed=0, gather=args.gather,

@@ -144,17 +144,19 @@ KLAB_API int klab_wait_flags(const unsigned* flags, int slot, int npeers, const 
 /* Persistent projection chain (no counterpart in the reference, whose chain is
  * one launch per projection, l2prefetch.py:38-60): every projection of a token
  * step in ONE cooperative launch, BF16 weights, one token. Stage s computes
- * the rows of its nseg weights w[i] [n[i], k] from the input x. Segment
- * gather_seg feeds the next stage: its outputs are written as 32-bit words
- * (tag << 16 | bf16) into every rank's gather buffer (peer_out[q], rank q's
- * buffer at this rank's first row; peer_out[rank] is the local one), over
- * NVLink for the peers. Stage 0's x is plain BF16; stage s > 0's x is the
- * local gather buffer of stage s-1 (tagged words, n[gather_seg] * npeers of
- * them). Other segments write plain BF16 to out[i]. Gather buffers start
- * zeroed. sync->final_in is the last stage's local gather buffer; the launch
- * ends after its plain BF16 values are in final_out. epoch (device u32, zero at
- * start) counts completed steps. Outputs are bit-identical to one
- * klab_gemv_multi launch per stage. One GPU: npeers = 1. */
+ * the rows of its nseg weights w[i] [n[i], k] from the input x: the plain BF16
+ * step input when x_stage = -1, else the local gather buffer of stage x_stage
+ * (an earlier stage). A stage's gather segment (gather_seg, -1: none) is
+ * written as 32-bit words (tag << 16 | bf16) into every rank's gather buffer
+ * (peer_out[q], rank q's buffer at this rank's first row; peer_out[rank] is the
+ * local one), over NVLink for the peers; other segments write plain BF16 to
+ * out[i]. A stage that rewrites a gather buffer must take its input from a
+ * stage after every reader of the buffer's previous content; every stage must
+ * have at least as many row x 2048-column items as the GPU has SMs. Gather
+ * buffers start zeroed. sync->final_in is the last gathering stage's local
+ * buffer; the launch ends after its plain BF16 values are in final_out. epoch
+ * (device u32, zero at start) counts completed steps. Outputs are
+ * bit-identical to one klab_gemv_multi launch per stage. One GPU: npeers = 1. */
 typedef struct klab_chain_stage {
   const void* x;
   int k;
@@ -164,6 +166,7 @@ typedef struct klab_chain_stage {
   int n[8];
   int gather_seg;
   void* peer_out[8];
+  int x_stage;
 } klab_chain_stage_t;
 
 typedef struct klab_chain_sync {
@@ -183,7 +186,8 @@ KLAB_API int klab_chain_destroy(void* plan);
 /* Launch shape of a plan: CTAs and trace slots per (stage, CTA). */
 KLAB_API int klab_chain_info(void* plan, int* grid, int* trace_slots);
 /* Optional timeline: later launches write global-timer ns per (stage, CTA):
- * [entered, x staged, then each warp's last item] into buffer
+ * [entered, previous stage done in this CTA, x staged, then each warp's last
+ * item] into buffer
  * [nstages][grid][trace_slots] u64 (NULL: off). */
 KLAB_API int klab_chain_trace(void* plan, unsigned long long* buffer, size_t bytes);
 

@@ -237,7 +237,7 @@ class ChainStage(ct.Structure):
     """klab_chain_stage_t: one stage of the persistent chain kernel."""
 
     _fields_ = [("x", _P), ("k", _I), ("nseg", _I), ("w", _P * 8), ("out", _P * 8), ("n", _I * 8),
-                ("gather_seg", _I), ("peer_out", _P * MAX_PEERS)]
+                ("gather_seg", _I), ("peer_out", _P * MAX_PEERS), ("x_stage", _I)]
 
 
 class ChainSync(ct.Structure):

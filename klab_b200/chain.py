@@ -168,66 +168,105 @@ class ProjectionChain:
         if self.persistent:
             self._setup_persistent()
 
+    def persistent_schedule(self):
+        """Stages of the persistent kernel for one layer i, in order:
+        up (gathered into up_t; x = h_i), fill1 (first half of q, k, v, o, gate
+        rows; x = h_i), down (gathered into h_t[(i+1) % 2]; x = up_t), fill2
+        (the other half; x = h_i again). Only up and down feed later stages, so
+        each data dependency (up -> down, down -> next up) has a filler stage of
+        independent rows between producer and consumer. Returns, per layer, a
+        list of (kind, [(name, local_row_begin, local_row_end)])."""
+        names = [name for name, _ in self.shape.projections()[0] if name != "up"]
+        fill = []
+        for name in names:
+            n = self.layers[0][name][1][1] - self.layers[0][name][1][0]
+            fill.append((name, 0, n))
+        total = sum(e - b for _, b, e in fill)
+        half, fill1, fill2, acc = total // 2, [], [], 0
+        for name, b, e in fill:
+            if acc + (e - b) <= half:
+                fill1.append((name, b, e))
+            elif acc >= half:
+                fill2.append((name, b, e))
+            else:
+                cut = b + (half - acc)
+                fill1.append((name, b, cut))
+                fill2.append((name, cut, e))
+            acc += e - b
+        return [("up", [("up", 0, None)]), ("fill1", fill1), ("down", [("down", 0, None)]), ("fill2", fill2)]
+
     def _setup_persistent(self):
-        """Stage table of the persistent kernel: stage 2i = the six stage-A
-        projections of layer i (up feeds stage 2i+1), stage 2i+1 = down (feeds
-        the next layer). The up and down outputs live only as tagged words
-        (tag << 16 | bf16) in the gather buffers up_t [ffn] and h_t [hidden],
-        which every rank writes into (IPC mappings when world > 1)."""
+        """Stage table of the persistent kernel (persistent_schedule). The up and
+        down outputs live only as tagged words (tag << 16 | bf16) in the gather
+        buffers up_t [ffn] and h_t[2] [hidden], which every rank writes into
+        (IPC mappings when world > 1); layer i reads h_t[i % 2]."""
         shape, world, rank = self.shape, self.world, self.rank
         bf = dict(dtype=torch.bfloat16, device=self.device)
         self.hbuf = [torch.zeros((1, shape.hidden), **bf)]        # step input (plain BF16)
         self.out = torch.zeros((1, shape.hidden), **bf)           # step output (plain BF16)
         self.up_full = None
-        words = {"ht": shape.hidden * 4, "upt": shape.ffn * 4}
+        words = {"ht0": shape.hidden * 4, "ht1": shape.hidden * 4, "upt": shape.ffn * 4}
         if world == 1:
-            self.h_t = torch.zeros(shape.hidden, dtype=torch.int32, device=self.device)
-            self.up_t = torch.zeros(shape.ffn, dtype=torch.int32, device=self.device)
-            bases = {"ht": [self.h_t.data_ptr()], "upt": [self.up_t.data_ptr()]}
+            local = {name: torch.zeros(n // 4, dtype=torch.int32, device=self.device) for name, n in words.items()}
+            bases = {name: [t.data_ptr()] for name, t in local.items()}
         else:
             raw, offsets = self._ipc_region(words)
-            self.h_t = raw[offsets["ht"]:offsets["ht"] + words["ht"]].view(torch.int32)
-            self.up_t = raw[offsets["upt"]:offsets["upt"] + words["upt"]].view(torch.int32)
+            local = {name: raw[offsets[name]:offsets[name] + n].view(torch.int32) for name, n in words.items()}
             bases = {name: [a + offsets[name] for a in self._ipc["peers"]] for name in words}
+        self.h_t = [local["ht0"], local["ht1"]]
+        self.up_t = local["upt"]
         self.ctrl = torch.zeros(64, dtype=torch.int32, device=self.device)
         self.epoch = self.ctrl[0:1]
-        stages = []
+        stages, schedule = [], self.persistent_schedule()
+        prev_down = -1
         for i, entry in enumerate(self.layers):
-            st = _native.ChainStage()
-            st.x = (self.hbuf[0] if i == 0 else self.h_t).data_ptr()
-            st.k, st.nseg, st.gather_seg = shape.hidden, 6, 5
-            for j, name in enumerate(("q", "k", "v", "o", "gate", "up")):
-                w, rows, _ = entry[name]
-                st.w[j], st.n[j] = w.data_ptr(), rows[1] - rows[0]
-                if name != "up":
-                    st.out[j] = self.a_out[name][:, rows[0]:].data_ptr()
-            r0 = entry["up"][1][0]
-            for q in range(world):
-                st.peer_out[q] = bases["upt"][q] + r0 * 4
-            stages.append(st)
-            st = _native.ChainStage()
-            w, rows, _ = entry["down"]
-            st.x, st.k, st.nseg, st.gather_seg = self.up_t.data_ptr(), shape.ffn, 1, 0
-            st.w[0], st.n[0] = w.data_ptr(), rows[1] - rows[0]
-            for q in range(world):
-                st.peer_out[q] = bases["ht"][q] + rows[0] * 4
-            stages.append(st)
+            h_ptr = self.hbuf[0].data_ptr() if i == 0 else self.h_t[i % 2].data_ptr()
+            up_stage = None
+            for kind, parts in schedule:
+                st = _native.ChainStage()
+                st.gather_seg = -1
+                if kind == "up":
+                    w, rows, _ = entry["up"]
+                    st.x, st.k, st.x_stage, st.nseg, st.gather_seg = h_ptr, shape.hidden, prev_down, 1, 0
+                    st.w[0], st.n[0] = w.data_ptr(), rows[1] - rows[0]
+                    for q in range(world):
+                        st.peer_out[q] = bases["upt"][q] + rows[0] * 4
+                    up_stage = len(stages)
+                elif kind == "down":
+                    w, rows, _ = entry["down"]
+                    st.x, st.k, st.x_stage, st.nseg, st.gather_seg = self.up_t.data_ptr(), shape.ffn, up_stage, 1, 0
+                    st.w[0], st.n[0] = w.data_ptr(), rows[1] - rows[0]
+                    dst = "ht1" if i % 2 == 0 else "ht0"
+                    for q in range(world):
+                        st.peer_out[q] = bases[dst][q] + rows[0] * 4
+                    prev_down_next = len(stages)
+                else:
+                    st.x, st.k, st.x_stage, st.nseg = h_ptr, shape.hidden, prev_down, len(parts)
+                    for j, (name, b, e) in enumerate(parts):
+                        w, rows, _ = entry[name]
+                        st.w[j] = w[b:].data_ptr()
+                        st.out[j] = self.a_out[name][:, rows[0] + b:].data_ptr()
+                        st.n[j] = e - b
+                stages.append(st)
+            prev_down = prev_down_next
+        self._stage_kinds = [kind for _ in self.layers for kind, _ in schedule]
         sync = _native.ChainSync()
         sync.npeers, sync.rank = world, rank
         sync.epoch = self.epoch.data_ptr()
-        sync.final_in, sync.final_out = self.h_t.data_ptr(), self.out.data_ptr()
+        sync.final_in = self.h_t[len(self.layers) % 2].data_ptr()
+        sync.final_out = self.out.data_ptr()
         with torch.cuda.device(self.device):
             self._plan = _native.chain_create(stages, sync)
 
     def trace_step(self, x):
         """Run one eager step of the persistent kernel with its timeline on and
         return it as an int64 tensor [stages, CTAs, slots] of global-timer ns
-        (slots: entered, flags seen, x staged, warps done, flag published, then
-        each warp's last item)."""
+        (slots: entered, previous stage done in this CTA, x staged, then each
+        warp's last item)."""
         if not self.persistent:
             raise ValueError("trace_step needs persistent=True")
         grid, slots = _native.chain_info(self._plan)
-        buf = torch.zeros((2 * self.shape.layers, grid, slots), dtype=torch.int64, device=self.device)
+        buf = torch.zeros((len(self._stage_kinds), grid, slots), dtype=torch.int64, device=self.device)
         _native.chain_trace(self._plan, buf)
         try:
             self.forward_eager(x)

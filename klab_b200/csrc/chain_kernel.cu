@@ -43,8 +43,14 @@
 namespace klab {
 namespace {
 
-constexpr int kChainWarps = 16;
-constexpr int kChainDepth = 3;
+#ifndef KLAB_CHAIN_WARPS
+#define KLAB_CHAIN_WARPS 16
+#endif
+#ifndef KLAB_CHAIN_DEPTH
+#define KLAB_CHAIN_DEPTH 3
+#endif
+constexpr int kChainWarps = KLAB_CHAIN_WARPS;  // warps per CTA
+constexpr int kChainDepth = KLAB_CHAIN_DEPTH;  // ring slots per warp
 constexpr int kChainKC = Layout<W_BF16>::KC;  // 2048 columns per item
 constexpr int kChainSlot = kWeightSlot;       // 4096 bytes per item
 constexpr int kChainMaxK = 16384;             // x staging capacity (BF16 values)
@@ -62,11 +68,11 @@ struct ChainSeg {
 };
 
 struct ChainStage {
-  const void* x;         // stage 0: BF16 [k]; later stages: tagged words [k]
+  const void* x;         // plain BF16 [k] (x_stage < 0) or tagged words [k]
   int k, chunks, n, nseg;
   long long ws_off;      // this stage's tagged partials [n][S] (64-bit words)
-  int gather_seg;        // segment written as tagged words to every rank
-  int pad;
+  int gather_seg;        // segment written as tagged words to every rank (-1: none)
+  int x_stage;           // stage whose gathered output x is (-1: plain input)
   ChainSeg seg[kMaxSegs];
   unsigned* peer_out[kMaxPeers];  // rank q's tagged buffer, at gather_seg's first row
 };
@@ -79,14 +85,16 @@ struct ChainParams {
   unsigned* exits;                 // CTAs finished with the step, zero between steps
   unsigned long long* ws;          // tagged split-row partials
   int* status;
-  const unsigned* final_in;        // tagged output of the last stage
+  const unsigned* final_in;        // tagged output of stage final_stage
   unsigned short* final_out;       // its BF16 values
   int final_n;
+  int final_stage;
   unsigned long long* trace;       // optional: [nstages][grid][kTraceSlots] global-timer ns
 };
 
-// Trace slots per (stage, CTA): entered, x staged, then each warp's last item.
-constexpr int kTraceCta = 2;
+// Trace slots per (stage, CTA): entered, every warp done with the previous
+// stage, x staged, then each warp's last item.
+constexpr int kTraceCta = 3;
 constexpr int kTraceSlots = kTraceCta + kChainWarps;
 
 __device__ __forceinline__ unsigned long long global_ns() {
@@ -208,7 +216,7 @@ __device__ bool stage_chain_x(const ChainStage& st, bool tagged, unsigned tag, u
   // Four tagged words (16 bytes) -> four BF16 values (8 bytes) per vector.
   // All of a thread's vectors are loaded at once; only stale ones are re-read.
   const char* src = static_cast<const char*>(st.x);
-  constexpr int kPer = kChainMaxK / 4 / (kChainWarps * 32);  // vectors per thread at most
+  constexpr int kPer = (kChainMaxK / 4 + kChainWarps * 32 - 1) / (kChainWarps * 32);  // vectors per thread
   const int nvec = segs * 64;
   uint4 v[kPer];
   bool fresh[kPer];
@@ -315,6 +323,8 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
   __syncwarp();
 
   const unsigned epoch = *p.epoch + 1u;  // this step
+  const void* staged_x = nullptr;        // input now in xs (the same in every thread)
+  int staged_from = -2;
   bool ok = true;
   long long g = 0;        // ring position of the next item to consume
   long long failed = -1;  // ring position of a copy that never completed
@@ -328,13 +338,19 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
     if (threadIdx.x == 0) trace_mark(p, s, 0);
     // Barrier (every warp is done with the previous x); stage x if any warp
     // of this CTA has items in this stage.
-    if (__syncthreads_or(nitems > 0 ? 1 : 0)) {
-      const bool tagged = s > 0;
-      if (!stage_chain_x(st, tagged, tagged ? stage_tag(epoch, p.nstages, s - 1) : 0u, xs, &s_broken))
+    const bool need = __syncthreads_or(nitems > 0 ? 1 : 0);
+    if (threadIdx.x == 0) trace_mark(p, s, 1);
+    // Stage x unless this CTA holds no item of the stage or x is already there
+    // (the same input as the previous staging).
+    if (need && (st.x != staged_x || st.x_stage != staged_from)) {
+      const bool tagged = st.x_stage >= 0;
+      if (!stage_chain_x(st, tagged, tagged ? stage_tag(epoch, p.nstages, st.x_stage) : 0u, xs, &s_broken))
         record_status(p.status, kStatusFlagTimeout);
+      staged_x = st.x;
+      staged_from = st.x_stage;
       __syncthreads();
     }
-    if (threadIdx.x == 0) trace_mark(p, s, 1);
+    if (threadIdx.x == 0) trace_mark(p, s, 2);
     const unsigned tag = stage_tag(epoch, p.nstages, s);
 
     int row = 0, c = 0;
@@ -391,7 +407,7 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
 
   // CTA 0 publishes the step's output once every rank's last-stage words are in.
   if (blockIdx.x == 0) {
-    const unsigned tag = stage_tag(epoch, p.nstages, p.nstages - 1);
+    const unsigned tag = stage_tag(epoch, p.nstages, p.final_stage);
     const unsigned long long t0 = global_ns();
     for (int j = threadIdx.x; j < p.final_n; j += blockDim.x) {
       unsigned v = 0;
@@ -456,10 +472,16 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
     if (!in.x || in.k <= 0 || in.k > kChainMaxK || in.k % 8 || in.nseg < 1 || in.nseg > kMaxSegs)
       return KLAB_E_SHAPE;
     if (reinterpret_cast<uintptr_t>(in.x) & 15) return KLAB_E_ALIGN;
-    // Every stage feeds the next (or the step output) through its gathered segment.
-    if (in.gather_seg < 0 || in.gather_seg >= in.nseg) return KLAB_E_INVALID;
-    if (s > 0 && in.k != stages[s - 1].n[stages[s - 1].gather_seg] * sync->npeers) return KLAB_E_SHAPE;
+    if (in.gather_seg < -1 || in.gather_seg >= in.nseg) return KLAB_E_INVALID;
+    // x is the plain step input or the gathered output of an earlier stage.
+    if (in.x_stage >= s || in.x_stage < -1) return KLAB_E_INVALID;
+    if (in.x_stage >= 0) {
+      const klab_chain_stage_t& src = stages[in.x_stage];
+      if (src.gather_seg < 0) return KLAB_E_INVALID;
+      if (in.k != src.n[src.gather_seg] * sync->npeers) return KLAB_E_SHAPE;
+    }
     st.x = in.x;
+    st.x_stage = in.x_stage;
     st.k = in.k;
     st.chunks = (in.k + kChainKC - 1) / kChainKC;
     st.nseg = in.nseg;
@@ -473,7 +495,7 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
       st.seg[i].row0 = rows;
       rows += in.n[i];
     }
-    for (int q = 0; q < sync->npeers; ++q) {
+    for (int q = 0; q < sync->npeers && in.gather_seg >= 0; ++q) {
       if (!in.peer_out[q] || (reinterpret_cast<uintptr_t>(in.peer_out[q]) & 3)) return KLAB_E_INVALID;
       st.peer_out[q] = static_cast<unsigned*>(in.peer_out[q]);
     }
@@ -493,6 +515,15 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kChainWarps * 32, kChainSmem);
   if (err != cudaSuccess) return err;
   if (per_sm < 1) return KLAB_E_UNSUPPORTED;
+  // Every CTA holds items of every stage, so no CTA can still be reading a
+  // gather buffer when a later stage rewrites it (the rewriting stage's input
+  // is only complete once every CTA has passed the reading stages).
+  int final_stage = -1;
+  for (int s = 0; s < nstages; ++s) {
+    if (static_cast<long long>(host[s].n) * host[s].chunks < sms) return KLAB_E_SHAPE;
+    if (host[s].gather_seg >= 0) final_stage = s;
+  }
+  if (final_stage < 0) return KLAB_E_INVALID;
 
   ChainPlan* plan = new ChainPlan();
   plan->grid = sms;
@@ -521,7 +552,8 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
   p.status = device_status_address();
   p.final_in = sync->final_in;
   p.final_out = static_cast<unsigned short*>(sync->final_out);
-  p.final_n = stages[nstages - 1].n[stages[nstages - 1].gather_seg] * sync->npeers;
+  p.final_stage = final_stage;
+  p.final_n = stages[final_stage].n[stages[final_stage].gather_seg] * sync->npeers;
   *plan_out = plan;
   return 0;
 }

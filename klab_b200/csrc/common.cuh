@@ -80,6 +80,12 @@ __device__ __forceinline__ void bulk_g2s(unsigned dst, const void* src, unsigned
       : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (no destination, no completion
+// signal). src and bytes must be multiples of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // Orders this thread's earlier generic-proxy shared-memory accesses before later
 // async-proxy (bulk copy) writes to the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {
