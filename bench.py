@@ -284,6 +284,11 @@ def bench_projections(torch, peak, quick=False):
 
 # ---------------------------------------------------------------- dominant kernel roofline
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate launch (14336 x 4096 BF16,
+# M=1), mean of the two launches captured for profiles/stream_gemv_gate_bf16_m1.md.
+NCU_GATE_TRAFFIC_BYTES = 117_492_224 + 4_048_640
+
+
 def bench_dominant_kernel(torch, chain, peak, rounds=10):
     """Average duration of the chain's gate projection (the largest BF16 GEMV),
     timed with CUDA events on its launch stream over the chain's 32 distinct gate
@@ -303,12 +308,17 @@ def bench_dominant_kernel(torch, chain, peak, rounds=10):
                          h.shape[0], n_shard, shape.hidden, ldo=n)
 
     g = graph_of(torch, run, stream)
+    torch.cuda.nvtx.range_push("dominant")   # ncu --nvtx-include "dominant/" selects these launches
     us = time_graph(torch, g, len(gates), rounds)
+    torch.cuda.nvtx.range_pop()
     del g
     nbytes = n_shard * shape.hidden * 2 + shape.hidden * 2 + n_shard * 2
     achieved = nbytes / us / 1e3
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "traffic": None, "kernel": "stream_gemv_kernel<W_BF16,X_BF16,SMEM,1>",
+            "frac": round(achieved / peak, 4),
+            "traffic": NCU_GATE_TRAFFIC_BYTES if chain.world == 1 else None,
+            "traffic_unit": "bytes per launch (ncu capture, profiles/stream_gemv_gate_bf16_m1.md)",
+            "kernel": "stream_gemv_kernel<W_BF16,X_BF16,SMEM16,1>",
             "launch": f"gate {n_shard}x{shape.hidden} bf16, M=1", "bytes_per_launch": nbytes,
             "us_per_launch": round(us, 3)}
 
@@ -434,10 +444,12 @@ def main(argv=None):
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0 = time.perf_counter()
+    torch.cuda.nvtx.range_push("chain")      # the timed token steps
     e0.record(stream)
     for _ in range(args.steps):
         chain.replay()
     e1.record(stream)
+    torch.cuda.nvtx.range_pop()
     e1.synchronize()
     t1 = time.perf_counter()
     barrier(world)
