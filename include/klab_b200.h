@@ -54,6 +54,8 @@ extern "C" {
 #define KLAB_W_I8_G64 5    /* int8 [N,K] + fp32 scale [N,K/64] */
 #define KLAB_W_FP4_G32H 6  /* E2M1 [N,K/2] (low nibble = even k) + fp16 scale [N,K/32] */
 #define KLAB_W_FP4_G16E 7  /* E2M1 [N,K/2] + E4M3 scale [N,K/16] + fp32 global scale */
+#define KLAB_W_LF32 8      /* lossless FP32 v1: 3-byte mantissa + exponent stream (lossless_weights.py) */
+#define KLAB_W_FP28 9      /* lossless FP32 as 28-bit codes (packed_fp32.py) */
 
 /* FP4 scale kinds (klab_fp4_linear / klab_fp4_dequantize). */
 #define KLAB_FP4_E4M3_G16 0
@@ -101,6 +103,23 @@ KLAB_API int klab_gemv_multi(int wfmt, int xdtype, const void* x, int ldx, int n
                              const void* const* aux, const float* gscale, void* const* out, const int* ldo,
                              const int* n, int out_dtype, int m, int k, void* workspace, size_t workspace_bytes,
                              void* stream);
+
+/* Lossless FP32 projections (FP32 x, FP32 out); results are bit-identical to
+ * klab_f32_linear on the decoded weights. Replace lossless_weights.fused_linear
+ * (lossless_weights.py:78-116, kernels lossless_t* in lossless_kernels.cu:41-65)
+ * and packed_fp32.fused_linear (packed_fp32.py:70-88, kernels fp28_t* in
+ * adaptive_kernels.cu:78-99). Formats: klab_b200/csrc/lossless_f32.cuh. */
+KLAB_API int klab_lossless_f32_linear(const float* x, const uint8_t* mantissa, const uint8_t* exponents,
+                                      const int32_t* metadata, float* out, int m, int n, int k, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+KLAB_API int klab_fp28_linear(const float* x, const int32_t* payload, const int32_t* metadata, float* out, int m,
+                              int n, int k, void* workspace, size_t workspace_bytes, void* stream);
+/* Decode to FP32 [count] (count % 64 == 0): lossless_unpack / fp28_unpack
+ * (lossless_kernels.cu:31-37, adaptive_kernels.cu:70-75). */
+KLAB_API int klab_lossless_f32_unpack(const uint8_t* mantissa, const uint8_t* exponents, const int32_t* metadata,
+                                      float* out, long long count, void* stream);
+KLAB_API int klab_fp28_unpack(const int32_t* payload, const int32_t* metadata, float* out, long long count,
+                              void* stream);
 
 /* Output gather fused into a projection, over NVLink peer memory (no
  * counterpart in the reference, which has no multi-GPU code; it replaces the

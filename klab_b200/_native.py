@@ -21,7 +21,7 @@ PREFETCH_CUBIN = LIB_DIR / "prefetch_kernels.cubin"
 
 # include/klab_b200.h constants
 DT_BF16, DT_F16, DT_F32 = 0, 1, 2
-W_BF16, W_F16, W_F32, W_CBF16, W_I8_ROW, W_I8_G64, W_FP4_G32H, W_FP4_G16E = range(8)
+W_BF16, W_F16, W_F32, W_CBF16, W_I8_ROW, W_I8_G64, W_FP4_G32H, W_FP4_G16E, W_LF32, W_FP28 = range(10)
 FP4_E4M3_G16, FP4_F16_G32 = 0, 1
 L2_HINT, L2_HINT_LAST, L2_LOAD = 0, 1, 2
 OPT_PDL, OPT_SPLIT, OPT_GENERIC, OPT_CTAS_PER_SM = 0, 1, 2, 3
@@ -53,6 +53,10 @@ _SIGNATURES = {
     "klab_f32_linear": (_I, [_P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "klab_int8_linear": (_I, [_P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _P, _SZ, _P]),
     "klab_fp4_linear": (_I, [_P, _I, _P, _P, _I, _P, _P, _I, _I, _I, _I, _P, _SZ, _P]),
+    "klab_lossless_f32_linear": (_I, [_P, _P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
+    "klab_fp28_linear": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
+    "klab_lossless_f32_unpack": (_I, [_P, _P, _P, _P, ct.c_longlong, _P]),
+    "klab_fp28_unpack": (_I, [_P, _P, _P, ct.c_longlong, _P]),
     "klab_gemv_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
     "klab_cbf16_unpack": (_I, [_P, _P, _P, _I, _I, _P]),
     "klab_int8_dequantize": (_I, [_P, _P, _I, _P, _I, _I, _P]),

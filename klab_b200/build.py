@@ -31,7 +31,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
                      "-fvisibility=hidden", f"-I{INCLUDE}"]
 CUDA_SOURCES = ("capi.cu", "aux_kernels.cu", "prefetch_kernels.cu", "gemv_half.cu", "gemv_cbf16.cu",
-                "gemv_int8.cu", "gemv_fp4a.cu", "gemv_fp4b.cu", "noalloc.cu", "peer.cu", "chain_kernel.cu")
+                "gemv_int8.cu", "gemv_fp4a.cu", "gemv_fp4b.cu", "noalloc.cu", "peer.cu", "chain_kernel.cu",
+                "gemv_lossless.cu")
 CXX_SOURCES = ("driver_abi.cpp", "codec_host.cpp")
 EXPORTS = OUT / "exports.map"
 

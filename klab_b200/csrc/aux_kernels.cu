@@ -8,6 +8,7 @@
 #include <cstdint>
 
 #include "common.cuh"
+#include "lossless_f32.cuh"
 #include "klab_kernels.h"
 
 namespace klab {
@@ -95,6 +96,28 @@ __global__ void __launch_bounds__(256) fp4_dequant_kernel(const unsigned char* _
     scale = f16_to_f32(static_cast<const unsigned short*>(scales)[row * (k / 32) + col / 32]);
   }
   out[index] = mul_rn(e, scale);
+}
+
+// Lossless FP32 formats -> FP32, four weights per thread (exact bits).
+__global__ void __launch_bounds__(256) lossless_unpack_kernel(const unsigned char* __restrict__ mantissa,
+                                                              const unsigned char* __restrict__ exponents,
+                                                              const unsigned* __restrict__ payload,
+                                                              const unsigned* __restrict__ metadata,
+                                                              float* __restrict__ out, long long count) {
+  const long long idx = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * 4;
+  if (idx >= count) return;
+  const float4 v = mantissa ? lf32_load4(mantissa, exponents, metadata, idx) : fp28_load4(payload, metadata, idx);
+  *reinterpret_cast<float4*>(out + idx) = v;
+}
+
+cudaError_t launch_lossless_unpack(const void* mantissa, const void* exponents, const void* payload,
+                                   const unsigned* metadata, float* out, long long count, cudaStream_t stream) {
+  const long long blocks = (count / 4 + 255) / 256;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
+  lossless_unpack_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(
+      static_cast<const unsigned char*>(mantissa), static_cast<const unsigned char*>(exponents),
+      static_cast<const unsigned*>(payload), metadata, out, count);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_cbf16_unpack(const void* payload, const unsigned* metadata, void* out, int n, int k,

@@ -77,7 +77,9 @@ int dtype_bytes(int dt) { return dt == KLAB_DT_F32 ? 4 : 2; }
 
 int vals_of(int wfmt) {
   switch (wfmt) {
-    case W_F32: return 4;
+    case W_F32:
+    case W_LF32:
+    case W_FP28: return 4;
     case W_I8_ROW:
     case W_I8_G64: return 16;
     case W_FP4_G32H:
@@ -90,7 +92,9 @@ size_t warp_region_bytes(int wfmt) {
   switch (wfmt) {
     case W_BF16: return Layout<W_BF16>::WARP_BYTES;
     case W_F16: return Layout<W_F16>::WARP_BYTES;
-    case W_F32: return Layout<W_F32>::WARP_BYTES;
+    case W_F32:
+    case W_LF32:
+    case W_FP28: return Layout<W_F32>::WARP_BYTES;
     case W_CBF16: return Layout<W_CBF16>::WARP_BYTES;
     case W_I8_ROW: return Layout<W_I8_ROW>::WARP_BYTES;
     case W_I8_G64: return Layout<W_I8_G64>::WARP_BYTES;
@@ -116,6 +120,8 @@ cudaError_t run_family(int wfmt, const GemvParams& p, const LaunchShape& s, cuda
     case W_I8_G64: return gemv_run_int8(wfmt, p, s, stream, occ);
     case W_FP4_G32H: return gemv_run_fp4a(wfmt, p, s, stream, occ);
     case W_FP4_G16E: return gemv_run_fp4b(wfmt, p, s, stream, occ);
+    case W_LF32:
+    case W_FP28: return gemv_run_lossless(wfmt, p, s, stream, occ);
     default: return cudaErrorNotSupported;
   }
 }
@@ -156,7 +162,9 @@ bool x_compatible(int wfmt, int xdt) {
     case W_BF16:
     case W_CBF16: return xdt == KLAB_DT_BF16;
     case W_F16: return xdt == KLAB_DT_F16;
-    case W_F32: return xdt == KLAB_DT_F32;
+    case W_F32:
+    case W_LF32:
+    case W_FP28: return xdt == KLAB_DT_F32;
     default: return xdt == KLAB_DT_BF16 || xdt == KLAB_DT_F16 || xdt == KLAB_DT_F32;
   }
 }
@@ -164,7 +172,9 @@ bool x_compatible(int wfmt, int xdt) {
 int shape_ok(int wfmt, int k) {
   switch (wfmt) {
     case W_CBF16:
-    case W_I8_G64: return k % 64 == 0;
+    case W_I8_G64:
+    case W_LF32:
+    case W_FP28: return k % 64 == 0;
     case W_FP4_G32H: return k % 32 == 0;
     case W_FP4_G16E: return k % 16 == 0;
     default: return 1;
@@ -178,11 +188,12 @@ size_t workspace_need(int tiles, int mt, int n, int chunks) {
 int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const void* const* w,
                    const void* const* aux, const float* gscale, void* const* out, const int* ldo, const int* nrows,
                    int out_dt, int m, int k, void* ws, size_t ws_bytes, void* stream,
-                   const klab_gather_t* gather = nullptr) {
+                   const klab_gather_t* gather = nullptr, const void* const* aux2 = nullptr) {
   if (!x || !w || !out || !ldo || !nrows || nseg < 1 || nseg > kMaxSegs) return KLAB_E_INVALID;
   if (m <= 0 || k <= 0 || ldx < k) return KLAB_E_INVALID;
-  if (wfmt < W_BF16 || wfmt > W_FP4_G16E) return KLAB_E_UNSUPPORTED;
+  if (wfmt < W_BF16 || wfmt > W_FP28) return KLAB_E_UNSUPPORTED;
   if (!x_compatible(wfmt, xdt)) return KLAB_E_UNSUPPORTED;
+  if (wfmt == W_LF32 && !aux2) return KLAB_E_INVALID;
   if (out_dt != KLAB_DT_BF16 && out_dt != KLAB_DT_F32) return KLAB_E_UNSUPPORTED;
   const bool needs_aux = wfmt >= W_CBF16;
   if (wfmt == W_FP4_G16E && !gscale) return KLAB_E_INVALID;
@@ -191,6 +202,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   for (int i = 0; i < nseg; ++i) {
     if (!w[i] || !out[i] || nrows[i] <= 0 || ldo[i] < nrows[i]) return KLAB_E_INVALID;
     if (needs_aux && (!aux || !aux[i])) return KLAB_E_INVALID;
+    if (wfmt == W_LF32 && !aux2[i]) return KLAB_E_INVALID;
     total += nrows[i];
   }
   if (total >= (1ll << 31)) return KLAB_E_SHAPE;
@@ -285,6 +297,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   for (int i = 0; i < nseg; ++i) {
     p.seg[i].w = w[i];
     p.seg[i].aux = needs_aux ? aux[i] : nullptr;
+    p.seg[i].aux2 = aux2 ? aux2[i] : nullptr;
     p.seg[i].out = out[i];
     p.seg[i].ldo = ldo[i];
     p.seg[i].row0 = row0;
@@ -326,7 +339,8 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
              void* out, int ldo, int out_dt, int m, int n, int k, void* ws, size_t ws_bytes, void* stream) {
   if (!x || !w || !out) return KLAB_E_INVALID;
   if (m <= 0 || n <= 0 || k <= 0 || ldx < k || ldo < n) return KLAB_E_INVALID;
-  if (wfmt >= W_CBF16 && wfmt <= W_FP4_G16E && !aux) return KLAB_E_INVALID;
+  if (wfmt >= W_CBF16 && wfmt <= W_FP28 && !aux) return KLAB_E_INVALID;
+  if (wfmt == W_LF32) return KLAB_E_UNSUPPORTED;  // needs the exponent stream: klab_lossless_f32_linear
   const void* ws_[1] = {w};
   const void* as_[1] = {aux};
   void* os_[1] = {out};
@@ -396,6 +410,46 @@ int klab_fp4_linear(const void* x, int xdtype, const uint8_t* packed, const void
                   workspace_bytes, stream);
 }
 
+int klab_lossless_f32_linear(const float* x, const uint8_t* mantissa, const uint8_t* exponents,
+                             const int32_t* metadata, float* out, int m, int n, int k, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  if (!x || !mantissa || !exponents || !metadata || !out || m <= 0 || n <= 0 || k <= 0) return KLAB_E_INVALID;
+  if (reinterpret_cast<uintptr_t>(mantissa) & 3u) return KLAB_E_ALIGN;
+  const void* w_[1] = {mantissa};
+  const void* a_[1] = {metadata};
+  const void* e_[1] = {exponents};
+  void* o_[1] = {out};
+  const int ldo_[1] = {n};
+  const int n_[1] = {n};
+  return run_gemv_multi(W_LF32, KLAB_DT_F32, x, k, 1, w_, a_, nullptr, o_, ldo_, n_, KLAB_DT_F32, m, k, workspace,
+                        workspace_bytes, stream, nullptr, e_);
+}
+
+int klab_fp28_linear(const float* x, const int32_t* payload, const int32_t* metadata, float* out, int m, int n,
+                     int k, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !payload || !metadata || !out) return KLAB_E_INVALID;
+  if (reinterpret_cast<uintptr_t>(payload) & 3u) return KLAB_E_ALIGN;
+  return run_gemv(W_FP28, KLAB_DT_F32, x, k, payload, metadata, nullptr, out, n, KLAB_DT_F32, m, n, k, workspace,
+                  workspace_bytes, stream);
+}
+
+int klab_lossless_f32_unpack(const uint8_t* mantissa, const uint8_t* exponents, const int32_t* metadata, float* out,
+                             long long count, void* stream) {
+  if (!mantissa || !exponents || !metadata || !out || count <= 0) return KLAB_E_INVALID;
+  if (count % 64) return KLAB_E_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(mantissa) & 3u) || (reinterpret_cast<uintptr_t>(out) & 15u)) return KLAB_E_ALIGN;
+  return launch_lossless_unpack(mantissa, exponents, nullptr, reinterpret_cast<const unsigned*>(metadata), out,
+                                count, static_cast<cudaStream_t>(stream));
+}
+
+int klab_fp28_unpack(const int32_t* payload, const int32_t* metadata, float* out, long long count, void* stream) {
+  if (!payload || !metadata || !out || count <= 0) return KLAB_E_INVALID;
+  if (count % 64) return KLAB_E_SHAPE;
+  if (reinterpret_cast<uintptr_t>(out) & 15u) return KLAB_E_ALIGN;
+  return launch_lossless_unpack(nullptr, nullptr, payload, reinterpret_cast<const unsigned*>(metadata), out, count,
+                                static_cast<cudaStream_t>(stream));
+}
+
 int klab_gemv_multi(int wfmt, int xdtype, const void* x, int ldx, int nseg, const void* const* w,
                     const void* const* aux, const float* gscale, void* const* out, const int* ldo, const int* n,
                     int out_dtype, int m, int k, void* workspace, size_t workspace_bytes, void* stream) {
@@ -412,7 +466,7 @@ int klab_gemv_multi_gather(int wfmt, int xdtype, const void* x, int ldx, int nse
 }
 
 size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k) {
-  if (wfmt < W_BF16 || wfmt > W_FP4_G16E || m <= 0 || n <= 0 || k <= 0) return 0;
+  if (wfmt < W_BF16 || wfmt > W_FP28 || m <= 0 || n <= 0 || k <= 0) return 0;
   const int kc = 256 * vals_of(wfmt);
   const int chunks = (k + kc - 1) / kc;
   if (chunks < 2 || static_cast<size_t>(n) > kTicketCap) return 0;

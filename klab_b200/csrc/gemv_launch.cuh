@@ -88,5 +88,6 @@ cudaError_t gemv_run_cbf16(int wfmt, const GemvParams& p, const LaunchShape& s, 
 cudaError_t gemv_run_int8(int wfmt, const GemvParams& p, const LaunchShape& s, cudaStream_t stream, int* occ);
 cudaError_t gemv_run_fp4a(int wfmt, const GemvParams& p, const LaunchShape& s, cudaStream_t stream, int* occ);
 cudaError_t gemv_run_fp4b(int wfmt, const GemvParams& p, const LaunchShape& s, cudaStream_t stream, int* occ);
+cudaError_t gemv_run_lossless(int wfmt, const GemvParams& p, const LaunchShape& s, cudaStream_t stream, int* occ);
 
 }  // namespace klab

@@ -9,6 +9,11 @@
 //   W_I8_G64  int8 + fp32 scale per 64 (int8_kernels.cu, int8_weights.py:23-35)
 //   W_FP4_G32H E2M1 + fp16 scale per 32
 //   W_FP4_G16E E2M1 + E4M3 scale per 16 + fp32 global (fp4_kernels.cu, fp4.py:33-60)
+//   W_LF32    lossless FP32 v1 (lossless_kernels.cu, lossless_weights.py)
+//   W_FP28    lossless FP32 as 28-bit codes (adaptive_kernels.cu fp28, packed_fp32.py)
+// The two lossless FP32 formats are decoded to their exact FP32 bits while a warp
+// fills its slot (cooperative fill, no bulk copy) and then use W_F32's arithmetic,
+// so their results are bit-identical to the FP32 projection of the same weights.
 //
 // Data movement (B200): every warp owns a private ring of DEPTH shared-memory
 // slots filled by 1-D bulk copies (cp.async.bulk into this CTA only) with mbarrier
@@ -38,6 +43,7 @@
 // the same bits as one warp doing the whole row.
 #pragma once
 #include "common.cuh"
+#include "lossless_f32.cuh"
 
 namespace klab {
 
@@ -50,6 +56,8 @@ enum WFmt : int {
   W_I8_G64 = 5,
   W_FP4_G32H = 6,
   W_FP4_G16E = 7,
+  W_LF32 = 8,      // lossless FP32 v1 (3-byte mantissa + exponent stream), decoded into the slot
+  W_FP28 = 9,      // lossless FP32 in 28-bit codes, decoded into the slot
 };
 enum XFmt : int { X_BF16 = 0, X_F16 = 1, X_F32 = 2 };
 // Where x lives while the tile is computed.
@@ -110,6 +118,14 @@ template <>
 struct WTraits<W_FP4_G16E> {
   static constexpr int VALS = 32, NUM = 1, DEN = 2, SCALE_BYTES = 512;
 };
+template <>
+struct WTraits<W_LF32> {
+  static constexpr int VALS = 4, NUM = 4, DEN = 1, SCALE_BYTES = 0;
+};
+template <>
+struct WTraits<W_FP28> {
+  static constexpr int VALS = 4, NUM = 4, DEN = 1, SCALE_BYTES = 0;
+};
 
 template <int F>
 struct Layout {
@@ -128,6 +144,7 @@ constexpr int kMaxSegs = 8;
 struct Segment {
   const void* w;    // weights, codes or coded payload
   const void* aux;  // coded metadata (u32) / scales
+  const void* aux2; // W_LF32: exponent stream
   void* out;        // out[t * ldo + local row]
   int ldo;
   int row0;         // first launch row of this segment
@@ -174,6 +191,7 @@ struct GemvParams {
 struct RowRef {
   const char* w;
   const char* aux;
+  const char* aux2;
   int local;
   int seg;
 };
@@ -184,7 +202,7 @@ __device__ __forceinline__ RowRef resolve_row(const GemvParams& p, int row) {
   for (int i = 1; i < kMaxSegs; ++i)
     if (i < p.nseg && row >= p.seg[i].row0) s = i;
   return RowRef{static_cast<const char*>(p.seg[s].w), static_cast<const char*>(p.seg[s].aux),
-                row - p.seg[s].row0, s};
+                static_cast<const char*>(p.seg[s].aux2), row - p.seg[s].row0, s};
 }
 
 // ------------------------------------------------------------------ x staging
@@ -328,7 +346,7 @@ __device__ __forceinline__ void load_w(unsigned slot, unsigned meta_entry, unsig
       w[2 * i] = f16lo(q[i]);
       w[2 * i + 1] = f16hi(q[i]);
     }
-  } else if constexpr (F == W_F32) {
+  } else if constexpr (F == W_F32 || F == W_LF32 || F == W_FP28) {
     uint4 v = lds128(slot + (j * 32 + lane) * 16);
     w[0] = __uint_as_float(v.x);
     w[1] = __uint_as_float(v.y);
@@ -574,6 +592,23 @@ __device__ __forceinline__ void warp_copy_bytes(char* dst, const char* src, int 
 }
 
 
+// Fill of one slot with the exact FP32 values of a lossless-FP32 item: the
+// item's L weights start at flat index local * k + c * KC of the row's matrix;
+// lane l decodes weights 4l, 4l + 128, ... into the slot's natural order.
+template <int F>
+__device__ __forceinline__ void decode_f32_item(float* dst, const RowRef& r, int k, int c, int L, int lane) {
+  const long long first = static_cast<long long>(r.local) * k + static_cast<long long>(c) * Layout<F>::KC;
+  for (int i = lane * 4; i < L; i += 128) {
+    float4 v;
+    if constexpr (F == W_LF32)
+      v = lf32_load4(reinterpret_cast<const unsigned char*>(r.w), reinterpret_cast<const unsigned char*>(r.aux2),
+                     reinterpret_cast<const unsigned*>(r.aux), first + i);
+    else
+      v = fp28_load4(reinterpret_cast<const unsigned*>(r.w), reinterpret_cast<const unsigned*>(r.aux), first + i);
+    *reinterpret_cast<float4*>(dst + i) = v;
+  }
+}
+
 // ------------------------------------------------------------------ kernel
 
 // (row, chunk) position in a warp's item sequence.
@@ -785,7 +820,9 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
     } else {
       // Cooperative fill: any alignment, zero padding past the item's data.
       unsigned char* sp = slot0_ptr + (q % kDepth) * SLOT;
-      if constexpr (CODED) {
+      if constexpr (F == W_LF32 || F == W_FP28) {
+        decode_f32_item<F>(reinterpret_cast<float*>(sp), rref, k, c, L, lane);
+      } else if constexpr (CODED) {
         unsigned* ep = reinterpret_cast<unsigned*>(slot0_ptr + kDepth * SLOT + (q % kMetaRing) * kMetaEntry);
         const int nb = L / 64;
         if (lane < nb)

@@ -11,8 +11,8 @@ What runs here is the reference's Python, unmodified:
   * mtile_bf16.tile_for_m
   * int8_weights.quantize_weights / Int8Weights.dequantize,
     fp4.quantize_weights / FP4Weights.dequantize,
-    lossless_weights.pack_weights
-The three quantizers refuse non-CUDA tensors, and this container has no GPU.
+    lossless_weights.pack_weights, packed_fp32.pack_weights
+The quantizers and packers refuse non-CUDA tensors, and this container has no GPU.
 They run on CPU tensors here through a shim: a Tensor subclass whose .device
 reports "cuda" (so the device check passes) and a module-level torch proxy that
 drops device= arguments of the factory calls. Every tensor operation is still
@@ -175,6 +175,42 @@ def quant_fixtures(i8, fp4, lw):
     return out
 
 
+def lossless_cases():
+    """FP32 matrices that exercise both block kinds of the lossless formats."""
+    rng = np.random.default_rng(31)
+    cases = {}
+    w = rng.standard_normal((16, 192), dtype=np.float32) * np.float32(0.02)
+    w[0, :64] = np.float32(1.5)                                 # one exponent: delta 0 everywhere
+    w[1, 64:128] = np.float32(2.0) ** np.arange(-8, 8, 0.25, dtype=np.float32)[:64]  # deltas up to 15
+    w[2, :4] = [np.float32(np.inf), -np.float32(np.inf), np.float32(np.nan), -0.0]  # wide: exponent 255 and 0
+    w[3, 100] = np.float32(1e-40)                               # subnormal: exponent 0, wide block
+    w[4, 130] = np.float32(3e38)                                # huge
+    w[5, :] = 0.0                                               # all zero (narrow, base 0)
+    w[6, :64] = -np.float32(7.25)
+    cases["mixed"] = w
+    cases["normal"] = rng.standard_normal((8, 512), dtype=np.float32)
+    wide = rng.standard_normal((4, 128), dtype=np.float32) * np.exp2(rng.integers(-60, 60, (4, 128))).astype(np.float32)
+    cases["wide"] = wide.astype(np.float32)
+    return cases
+
+
+def lossless_fixtures(lw, pf):
+    """lossless_weights.pack_weights and packed_fp32.pack_weights, run as written."""
+    out = {}
+    for module in (lw, pf):
+        module.torch = _TorchProxy()
+    for name, w in lossless_cases().items():
+        out[f"{name}__w"] = w
+        lq = lw.pack_weights(torch.from_numpy(w.copy()).as_subclass(_CudaLooking))
+        out[f"{name}__lf32_mantissa"] = _plain(lq.mantissa)
+        out[f"{name}__lf32_exponents"] = _plain(lq.exponents)
+        out[f"{name}__lf32_metadata"] = _plain(lq.metadata)
+        pq = pf.pack_weights(torch.from_numpy(w.copy()).as_subclass(_CudaLooking))
+        out[f"{name}__fp28_payload"] = _plain(pq.payload)
+        out[f"{name}__fp28_metadata"] = _plain(pq.metadata)
+    return out
+
+
 def main():
     if not REFERENCE.is_dir():
         raise SystemExit(f"reference tree not found at {REFERENCE}")
@@ -187,6 +223,7 @@ def main():
     i8 = _load("int8_weights")
     fp4 = _load("fp4")
     lw = _load("lossless_weights")
+    pf = _load("packed_fp32")
 
     fixtures = {}
     fixtures.update(codec_fixtures(cb, br))
@@ -197,7 +234,8 @@ def main():
     fixtures["tile__kernel_count"] = np.array(len(mt.kernel_names()))
     np.savez_compressed(HERE / "reference_codec.npz", **fixtures)
     np.savez_compressed(HERE / "reference_quant.npz", **quant_fixtures(i8, fp4, lw))
-    for name in ("reference_codec.npz", "reference_quant.npz"):
+    np.savez_compressed(HERE / "reference_lossless.npz", **lossless_fixtures(lw, pf))
+    for name in ("reference_codec.npz", "reference_quant.npz", "reference_lossless.npz"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 

@@ -192,3 +192,49 @@ def test_cuda_scalar_division_semantics():
     c1, s1 = oq.int8_quantize_g64(w, "cuda")
     c2, s2 = oq.int8_quantize_g64(w, "cpu")
     assert np.abs(s1.view(np.int32).astype(np.int64) - s2.view(np.int32)).max() <= 1
+
+
+LOSSLESS_CASES = ("mixed", "normal", "wide")
+
+
+@pytest.fixture(scope="module")
+def lossless():
+    return np.load(GOLDEN / "reference_lossless.npz")
+
+
+@pytest.mark.parametrize("name", LOSSLESS_CASES)
+def test_lossless_f32_v1_pack_matches_reference(lossless, name):
+    """oracle.lossless.lf32_pack produces the reference packer's bytes
+    (lossless_weights.pack_weights), and unpacking restores every FP32 bit."""
+    from oracle import lossless as ol
+
+    w = lossless[f"{name}__w"]
+    mantissa, exponents, metadata = ol.lf32_pack(w)
+    np.testing.assert_array_equal(mantissa, lossless[f"{name}__lf32_mantissa"])
+    np.testing.assert_array_equal(exponents, lossless[f"{name}__lf32_exponents"])
+    np.testing.assert_array_equal(metadata, lossless[f"{name}__lf32_metadata"])
+    back = ol.lf32_unpack(mantissa, exponents, metadata)
+    np.testing.assert_array_equal(back.view(np.uint32), w.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", LOSSLESS_CASES)
+def test_fp28_pack_matches_reference(lossless, name):
+    """oracle.lossless.fp28_pack produces packed_fp32.pack_weights' words, and
+    unpacking restores every FP32 bit (NaN payloads, -0, infinities, subnormals)."""
+    from oracle import lossless as ol
+
+    w = lossless[f"{name}__w"]
+    payload, metadata = ol.fp28_pack(w)
+    np.testing.assert_array_equal(payload, lossless[f"{name}__fp28_payload"])
+    np.testing.assert_array_equal(metadata, lossless[f"{name}__fp28_metadata"])
+    back = ol.fp28_unpack(payload, metadata)
+    np.testing.assert_array_equal(back.view(np.uint32), w.view(np.uint32))
+
+
+def test_lossless_block_kinds_present(lossless):
+    """The fixtures hold both narrow (delta) and wide blocks of both formats."""
+    for name in LOSSLESS_CASES:
+        for fmt in ("lf32", "fp28"):
+            wide = lossless[f"{name}__{fmt}_metadata"].view(np.uint32) & 1
+            if name == "mixed":
+                assert wide.any() and not wide.all()
