@@ -121,6 +121,23 @@ KLAB_API int klab_lossless_f32_unpack(const uint8_t* mantissa, const uint8_t* ex
 KLAB_API int klab_fp28_unpack(const int32_t* payload, const int32_t* metadata, float* out, long long count,
                               void* stream);
 
+/* Prepared projection plans: validate a (format, x dtype, out dtype, M, N, K)
+ * case once and freeze its launch (token tile, x staging, grid, split-K, the
+ * split-K workspace, owned by the plan); launches then only bind pointers.
+ * Replaces the reference's native plan registry (native/prepared.cpp:155-413:
+ * make_plan / register_plan / launch / raw / coded), whose kernel name and grid
+ * are likewise a pure function of the prepared case. Pointers passed to
+ * klab_plan_launch must be 16-byte aligned (coded payload 32-byte); aux is the
+ * format's side data (metadata or scales), aux2 the W_LF32 exponent stream.
+ * Launches of one plan must not overlap on the GPU (they share its workspace).
+ * The plan belongs to the device that was current at klab_plan_create. */
+KLAB_API int klab_plan_create(int wfmt, int xdtype, int out_dtype, int m, int n, int k, void** plan);
+KLAB_API int klab_plan_launch(void* plan, const void* x, const void* w, const void* aux, const void* aux2,
+                              const float* gscale, void* out, void* stream);
+/* JSON description of the frozen launch into buffer (NUL-terminated). */
+KLAB_API int klab_plan_info(void* plan, char* buffer, size_t bytes);
+KLAB_API int klab_plan_destroy(void* plan);
+
 /* Output gather fused into a projection, over NVLink peer memory (no
  * counterpart in the reference, which has no multi-GPU code; it replaces the
  * per-layer NCCL all-gather of the sharded chain). Segment `seg`'s outputs are

@@ -58,6 +58,10 @@ _SIGNATURES = {
     "klab_lossless_f32_unpack": (_I, [_P, _P, _P, _P, ct.c_longlong, _P]),
     "klab_fp28_unpack": (_I, [_P, _P, _P, ct.c_longlong, _P]),
     "klab_gemv_workspace_bytes": (_SZ, [_I, _I, _I, _I]),
+    "klab_plan_create": (_I, [_I, _I, _I, _I, _I, _I, ct.POINTER(_P)]),
+    "klab_plan_launch": (_I, [_P, _P, _P, _P, _P, _P, _P, _P]),
+    "klab_plan_info": (_I, [_P, ct.c_char_p, _SZ]),
+    "klab_plan_destroy": (_I, [_P]),
     "klab_cbf16_unpack": (_I, [_P, _P, _P, _I, _I, _P]),
     "klab_int8_dequantize": (_I, [_P, _P, _I, _P, _I, _I, _P]),
     "klab_fp4_dequantize": (_I, [_P, _P, _I, _P, _P, _I, _I, _P]),
@@ -280,6 +284,29 @@ def chain_trace(plan: int, buffer) -> None:
 
 def chain_destroy(plan: int) -> None:
     check(lib().klab_chain_destroy(plan), "klab_chain_destroy")
+
+
+def plan_create(wfmt, xdt, out_dt, m, n, k) -> int:
+    """A prepared launch for one case on the current device (klab_plan_create)."""
+    plan = ct.c_void_p()
+    check(lib().klab_plan_create(wfmt, xdt, out_dt, m, n, k, ct.byref(plan)), "klab_plan_create")
+    return plan.value
+
+
+def plan_info(plan: int) -> str:
+    buf = ct.create_string_buffer(1024)
+    check(lib().klab_plan_info(plan, buf, len(buf)), "klab_plan_info")
+    return buf.value.decode()
+
+
+def plan_launch(plan: int, x, w, aux, aux2, gscale, out, stream) -> None:
+    ptr_or_none = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    check(lib().klab_plan_launch(plan, x.data_ptr(), w.data_ptr(), ptr_or_none(aux), ptr_or_none(aux2),
+                                 ptr_or_none(gscale), out.data_ptr(), stream.cuda_stream), "klab_plan_launch")
+
+
+def plan_destroy(plan: int) -> None:
+    check(lib().klab_plan_destroy(plan), "klab_plan_destroy")
 
 
 def ipc_malloc(nbytes: int):

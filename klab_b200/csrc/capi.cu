@@ -3,6 +3,7 @@
 // options and the per-device status word.
 #include <atomic>
 #include <cstdint>
+#include <cstdio>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -181,6 +182,14 @@ int shape_ok(int wfmt, int k) {
   }
 }
 
+// A launch planned once (klab_plan_create) and replayed with new pointers.
+struct PlannedLaunch {
+  int wfmt = 0;
+  GemvParams p{};
+  LaunchShape s{};
+  size_t ws_need = 0;  // split-K workspace the launch needs (0: no split)
+};
+
 size_t workspace_need(int tiles, int mt, int n, int chunks) {
   return kTicketCap * 4 + static_cast<size_t>(tiles) * mt * n * chunks * 4;
 }
@@ -188,7 +197,8 @@ size_t workspace_need(int tiles, int mt, int n, int chunks) {
 int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const void* const* w,
                    const void* const* aux, const float* gscale, void* const* out, const int* ldo, const int* nrows,
                    int out_dt, int m, int k, void* ws, size_t ws_bytes, void* stream,
-                   const klab_gather_t* gather = nullptr, const void* const* aux2 = nullptr) {
+                   const klab_gather_t* gather = nullptr, const void* const* aux2 = nullptr,
+                   PlannedLaunch* plan_out = nullptr) {
   if (!x || !w || !out || !ldo || !nrows || nseg < 1 || nseg > kMaxSegs) return KLAB_E_INVALID;
   if (m <= 0 || k <= 0 || ldx < k) return KLAB_E_INVALID;
   if (wfmt < W_BF16 || wfmt > W_FP28) return KLAB_E_UNSUPPORTED;
@@ -332,6 +342,13 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
     p.split = 0;
   }
   s.grid = dim3(grid_x, tiles, 1);
+  if (plan_out) {
+    plan_out->wfmt = wfmt;
+    plan_out->p = p;
+    plan_out->s = s;
+    plan_out->ws_need = split ? need : 0;
+    return 0;
+  }
   return run_family(wfmt, p, s, static_cast<cudaStream_t>(stream), nullptr);
 }
 
@@ -463,6 +480,102 @@ int klab_gemv_multi_gather(int wfmt, int xdtype, const void* x, int ldx, int nse
                            size_t workspace_bytes, void* stream) {
   return run_gemv_multi(wfmt, xdtype, x, ldx, nseg, w, aux, gscale, out, ldo, n, out_dtype, m, k, workspace,
                         workspace_bytes, stream, gather);
+}
+
+// ---------------------------------------------------------------- prepared plans
+
+struct Plan {
+  PlannedLaunch launch;
+  int device = -1;
+  int m = 0, n = 0, k = 0, xdtype = 0, out_dtype = 0;
+  void* ws = nullptr;
+};
+
+int klab_plan_create(int wfmt, int xdtype, int out_dtype, int m, int n, int k, void** plan_out) {
+  if (!plan_out) return KLAB_E_INVALID;
+  *plan_out = nullptr;
+  if (wfmt < W_BF16 || wfmt > W_FP28 || m <= 0 || n <= 0 || k <= 0) return KLAB_E_INVALID;
+  // Plan with stand-in addresses that satisfy every alignment the kernels use;
+  // launches check that the real pointers do too.
+  void* const fake = reinterpret_cast<void*>(static_cast<uintptr_t>(1) << 20);
+  const void* w_[1] = {fake};
+  const void* a_[1] = {fake};
+  const void* e_[1] = {fake};
+  void* o_[1] = {fake};
+  const int ldo_[1] = {n};
+  const int n_[1] = {n};
+  const size_t ws_bytes = klab_gemv_workspace_bytes(wfmt, m, n, k);
+  Plan* plan = new Plan();
+  int rc = run_gemv_multi(wfmt, xdtype, fake, k, 1, w_, a_, static_cast<const float*>(fake), o_, ldo_, n_,
+                          out_dtype, m, k, ws_bytes ? fake : nullptr, ws_bytes, nullptr, nullptr,
+                          wfmt == W_LF32 ? e_ : nullptr, &plan->launch);
+  if (rc == 0) rc = cudaGetDevice(&plan->device);
+  if (rc == 0 && plan->launch.ws_need) {
+    rc = cudaMalloc(&plan->ws, plan->launch.ws_need);
+    if (rc == 0) rc = cudaMemset(plan->ws, 0, plan->launch.ws_need);
+  }
+  if (rc) {
+    if (plan->ws) cudaFree(plan->ws);
+    delete plan;
+    return rc;
+  }
+  plan->m = m;
+  plan->n = n;
+  plan->k = k;
+  plan->xdtype = xdtype;
+  plan->out_dtype = out_dtype;
+  if (plan->ws) {
+    plan->launch.p.tickets = static_cast<unsigned*>(plan->ws);
+    plan->launch.p.ws = reinterpret_cast<float*>(static_cast<char*>(plan->ws) + kTicketCap * 4);
+  }
+  *plan_out = plan;
+  return 0;
+}
+
+int klab_plan_launch(void* plan_ptr, const void* x, const void* w, const void* aux, const void* aux2,
+                     const float* gscale, void* out, void* stream) {
+  Plan* plan = static_cast<Plan*>(plan_ptr);
+  if (!plan || !x || !w || !out) return KLAB_E_INVALID;
+  const int wfmt = plan->launch.wfmt;
+  if (wfmt >= W_CBF16 && !aux) return KLAB_E_INVALID;
+  if ((wfmt == W_LF32 && !aux2) || (wfmt == W_FP4_G16E && !gscale)) return KLAB_E_INVALID;
+  if (!aligned16(x) || !aligned16(w) || (aux && !aligned16(aux)) || (aux2 && !aligned16(aux2))) return KLAB_E_ALIGN;
+  if (wfmt == W_CBF16 && (reinterpret_cast<uintptr_t>(w) & 31u)) return KLAB_E_ALIGN;
+  GemvParams p = plan->launch.p;
+  p.x = x;
+  p.gscale = gscale;
+  p.seg[0].w = w;
+  p.seg[0].aux = wfmt >= W_CBF16 ? aux : nullptr;
+  p.seg[0].aux2 = aux2;
+  p.seg[0].out = out;
+  return run_family(wfmt, p, plan->launch.s, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int klab_plan_info(void* plan_ptr, char* buffer, size_t bytes) {
+  Plan* plan = static_cast<Plan*>(plan_ptr);
+  if (!plan || !buffer || bytes == 0) return KLAB_E_INVALID;
+  const LaunchShape& s = plan->launch.s;
+  const char* xmodes[] = {"smem_fp32", "global", "smem_16bit"};
+  const int warps = warps_for(s.mt);
+  const int len = std::snprintf(
+      buffer, bytes,
+      "{\"wfmt\": %d, \"xdtype\": %d, \"out_dtype\": %d, \"shape_mnk\": [%d, %d, %d], \"tile\": %d, "
+      "\"x_staging\": \"%s\", \"grid\": [%u, %u, 1], \"block\": [%d, 1, 1], \"dynamic_shared_bytes\": %zu, "
+      "\"split_k\": %s, \"workspace_bytes\": %zu, \"bulk_copy\": %s, \"pdl\": %s, \"device\": %d, "
+      "\"kernel\": \"stream_gemv_kernel<%d,%d,%d,%d>\"}",
+      plan->launch.wfmt, plan->xdtype, plan->out_dtype, plan->m, plan->n, plan->k, s.mt, xmodes[s.xmode],
+      s.grid.x, s.grid.y, warps * 32, s.smem, plan->launch.p.split ? "true" : "false", plan->launch.ws_need,
+      plan->launch.p.use_tma ? "true" : "false", s.pdl ? "true" : "false", plan->device, plan->launch.wfmt,
+      s.xfmt, s.xmode, s.mt);
+  return (len < 0 || static_cast<size_t>(len) >= bytes) ? KLAB_E_SHAPE : 0;
+}
+
+int klab_plan_destroy(void* plan_ptr) {
+  Plan* plan = static_cast<Plan*>(plan_ptr);
+  if (!plan) return KLAB_E_INVALID;
+  if (plan->ws) cudaFree(plan->ws);
+  delete plan;
+  return 0;
 }
 
 size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k) {

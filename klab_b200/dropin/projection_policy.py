@@ -1,0 +1,9 @@
+"""Top-level name of the reference module `projection_policy`, served by klab_b200.projection_policy.
+
+Put klab_b200/dropin on sys.path ahead of the reference tree and `import projection_policy`
+resolves to the B200 implementation."""
+
+from klab_b200.projection_policy import *  # noqa: F401,F403
+from klab_b200 import projection_policy as _impl
+
+globals().update({k: v for k, v in vars(_impl).items() if not k.startswith("__")})

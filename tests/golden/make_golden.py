@@ -11,7 +11,8 @@ What runs here is the reference's Python, unmodified:
   * mtile_bf16.tile_for_m
   * int8_weights.quantize_weights / Int8Weights.dequantize,
     fp4.quantize_weights / FP4Weights.dequantize,
-    lossless_weights.pack_weights, packed_fp32.pack_weights
+    lossless_weights.pack_weights, packed_fp32.pack_weights,
+    projection_policy.choose (decisions on synthetic held-out reports)
 The quantizers and packers refuse non-CUDA tensors, and this container has no GPU.
 They run on CPU tensors here through a shim: a Tensor subclass whose .device
 reports "cuda" (so the device check passes) and a module-level torch proxy that
@@ -211,6 +212,62 @@ def lossless_fixtures(lw, pf):
     return out
 
 
+def policy_reports():
+    """Synthetic held-out reports in the reference's format: every branch of choose()."""
+    def case(seed, selected="warp_t128_v4", gain=(12.0, 15.0), aa=0.4, ok=True, half=False, shape=(1, 4096, 4096)):
+        c = {"shape_mnk": list(shape), "seed": seed, "selected": selected, "candidate_gain_ci95_pct": list(gain),
+             "aa_time_saved_pct": aa,
+             "methods": {"torch_mm": {"median_us": 30.0 + seed}, "cublas_mv": {"median_us": 25.0 + seed},
+                         "cublas_compute32": {"median_us": 28.0}, "torch_mm_out_fp32": {"median_us": 27.0}}}
+        if half:
+            c.update(bitwise_layout_check=ok, numerics_passed=ok, noise_gated_win=ok)
+        else:
+            c.update(bitwise_round_trip=ok, accepted_custom_win=ok)
+        return c
+
+    base = {"kind": "streaming-projection", "status": "complete"}
+    reports = {
+        "custom_pass": dict(base, cases=[case(1), case(2)]),
+        "custom_small_gain": dict(base, cases=[case(1, gain=(3.0, 5.0)), case(2, gain=(4.0, 6.0))]),
+        "one_seed": dict(base, cases=[case(1), case(1)]),
+        "noisy_aa": dict(base, cases=[case(1, aa=2.5), case(2)]),
+        "failed_check": dict(base, cases=[case(1, ok=False), case(2)]),
+        "lossless": dict(base, cases=[case(1, selected="lossless_t128"), case(2, selected="lossless_t128")]),
+        "other_shape": dict(base, cases=[case(1, shape=(2, 64, 64))]),
+        "half_pass": {"kind": "half-projection", "status": "complete", "mode": "validate", "dtype": "bf16",
+                      "cases": [case(1, "t128_v8", half=True), case(2, "t128_v8", half=True)]},
+        "compressed": {"kind": "compressed-projection", "output_dtype": "bf16",
+                       "cases": [{"shape_mnk": [1, 4096, 4096], "time_saved_pct": -3.0}]},
+        "compressed_ok": {"kind": "compressed-projection-validation", "output_dtype": "fp32", "cases": []},
+    }
+    return reports
+
+
+def policy_fixtures(pp):
+    out = {"reports": policy_reports(), "decisions": {}}
+    for name, report in out["reports"].items():
+        for force in (False, True):
+            try:
+                decision = pp.choose(report, (1, 4096, 4096), force_vendor=force,
+                                     output_dtype="bf16" if name == "compressed" else None)
+            except ValueError as exc:
+                decision = {"error": str(exc)}
+            out["decisions"][f"{name}__force{int(force)}"] = decision
+    for name, report in (("bad_selected", {"kind": "streaming-projection", "status": "complete",
+                                           "cases": [{"shape_mnk": [1, 4096, 4096], "seed": 1, "selected": "a"},
+                                                     {"shape_mnk": [1, 4096, 4096], "seed": 2, "selected": "b"}]}),
+                         ("bad_config", {"kind": "streaming-projection", "status": "complete",
+                                         "cases": [{"shape_mnk": [1, 4096, 4096], "seed": 1, "selected": "zz"}]}),
+                         ("incomplete", {"kind": "streaming-projection", "status": "running", "cases": []})):
+        out["reports"][name] = report
+        try:
+            decision = pp.choose(report, (1, 4096, 4096))
+        except ValueError as exc:
+            decision = {"error": str(exc)}
+        out["decisions"][f"{name}__force0"] = decision
+    return out
+
+
 def main():
     if not REFERENCE.is_dir():
         raise SystemExit(f"reference tree not found at {REFERENCE}")
@@ -224,6 +281,7 @@ def main():
     fp4 = _load("fp4")
     lw = _load("lossless_weights")
     pf = _load("packed_fp32")
+    pp = _load("projection_policy")
 
     fixtures = {}
     fixtures.update(codec_fixtures(cb, br))
@@ -235,7 +293,10 @@ def main():
     np.savez_compressed(HERE / "reference_codec.npz", **fixtures)
     np.savez_compressed(HERE / "reference_quant.npz", **quant_fixtures(i8, fp4, lw))
     np.savez_compressed(HERE / "reference_lossless.npz", **lossless_fixtures(lw, pf))
-    for name in ("reference_codec.npz", "reference_quant.npz", "reference_lossless.npz"):
+    import json
+
+    (HERE / "reference_policy.json").write_text(json.dumps(policy_fixtures(pp), indent=1, sort_keys=True) + "\n")
+    for name in ("reference_codec.npz", "reference_quant.npz", "reference_lossless.npz", "reference_policy.json"):
         print(name, (HERE / name).stat().st_size, "bytes")
 
 
