@@ -81,6 +81,8 @@ extern "C" {
 #define KLAB_OPT_SPLIT 1      /* -1 (default) automatic, 0 never, 1 always (when workspace allows) */
 #define KLAB_OPT_GENERIC 2    /* 1: force the cooperative-load (non bulk-copy) fill path */
 #define KLAB_OPT_CTAS_PER_SM 3 /* cap on projection CTAs per SM (0, default: as many as fit) */
+#define KLAB_OPT_TENSOR 4      /* token tiles on tcgen05 tensor cores: 0 never, 1 (default) INT8 per-row
+                                  weights at M >= 16, 2 INT8 per-row and BF16 weights at M >= 2 */
 
 /* ---------------------------------------------------------------- projections */
 

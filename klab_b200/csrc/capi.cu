@@ -18,7 +18,7 @@ __device__ int g_status_word;
 
 namespace {
 
-constexpr size_t kXSmemCap = 96 * 1024;       // x staging budget per CTA
+constexpr size_t kXSmemMin = 16 * 1024;       // smallest x staging budget considered
 #ifndef KLAB_PREFER_X16
 #define KLAB_PREFER_X16 KLAB_MIXED_BF16      // stage 16-bit x unconverted for 16-bit weights
 #endif
@@ -32,6 +32,11 @@ std::atomic<int> g_opt_pdl{1};
 std::atomic<int> g_opt_split{-1};
 std::atomic<int> g_opt_generic{0};
 std::atomic<int> g_opt_ctas_per_sm{0};  // 0: as many as fit
+// Tensor-core path for token tiles: 0 off; 1 (default) INT8 per-row weights at
+// M >= 16, where the tile is a dense contraction; 2 INT8 per-row and BF16 weights
+// at M >= 2 (BF16 M-tiles then differ from M = 1 in the last bits; the
+// CUDA-core M-tiles are bit-identical to M = 1).
+std::atomic<int> g_opt_tensor{1};
 
 struct DeviceInfo {
   bool ready = false;
@@ -242,15 +247,31 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
     }
   }
   const bool gathered_x = gather && gather->npeers > 0 && gather->wait_flags;
+  // Token tiles of INT8 (and, optionally, BF16) weights go to the tensor cores.
+  const int tensor = g_opt_tensor.load();
+  if (!plan_out && m >= 2 && nseg == 1 && !gather && xdt == KLAB_DT_BF16 &&
+      ((wfmt == W_I8_ROW && (tensor == 2 || (tensor == 1 && m >= 16))) || (wfmt == W_BF16 && tensor == 2))) {
+    const int rc_tc = tc_gemm_launch(wfmt == W_I8_ROW ? 1 : 0, x, ldx, w[0], wfmt == W_I8_ROW ?
+                                     static_cast<const float*>(aux[0]) : nullptr, out[0], ldo[0],
+                                     out_dt == KLAB_DT_F32, m, nrows[0], k, info->status,
+                                     static_cast<cudaStream_t>(stream));
+    if (rc_tc != KLAB_E_ALIGN) return rc_tc;  // misaligned operands fall through to the CUDA cores
+  }
   int mt = tile_for(m);
   int xmode = XM_SMEM;
-  const bool x16 = KLAB_PREFER_X16 && (wfmt == W_BF16 || wfmt == W_F16 || wfmt == W_CBF16) && xdt != KLAB_DT_F32;
+  // 16-bit x is staged unconverted; the x budget is what the rings leave of the
+  // CTA's shared memory, so wide token tiles keep x on chip instead of
+  // re-reading it from L1 for every item.
+  const bool x16 = KLAB_PREFER_X16 && xdt != KLAB_DT_F32;
   for (;;) {
-    if (x16 && static_cast<size_t>(mt) * kpad * 2 <= kXSmemCap) {
+    const int w_ = warps_for(mt);
+    const size_t rings = bar_region_bytes(wfmt, w_) + static_cast<size_t>(w_) * warp_region_bytes(wfmt);
+    const size_t cap = rings + kXSmemMin < kMaxSmem ? kMaxSmem - rings : kXSmemMin;
+    if (x16 && static_cast<size_t>(mt) * kpad * 2 <= cap) {
       xmode = XM_SMEM16;
       break;
     }
-    if (!x16 && static_cast<size_t>(mt) * kpad * 4 <= kXSmemCap) {
+    if (!x16 && static_cast<size_t>(mt) * kpad * 4 <= cap) {
       xmode = XM_SMEM;
       break;
     }
@@ -639,6 +660,10 @@ int klab_set_option(int option, int value) {
       if (value < 0 || value > 32) return KLAB_E_INVALID;
       g_opt_ctas_per_sm.store(value);
       return 0;
+    case KLAB_OPT_TENSOR:
+      if (value < 0 || value > 2) return KLAB_E_INVALID;
+      g_opt_tensor.store(value);
+      return 0;
     default: return KLAB_E_INVALID;
   }
 }
@@ -647,6 +672,7 @@ int klab_get_option(int option) {
   switch (option) {
     case KLAB_OPT_PDL: return g_opt_pdl.load();
     case KLAB_OPT_SPLIT: return g_opt_split.load();
+    case KLAB_OPT_TENSOR: return g_opt_tensor.load();
     case KLAB_OPT_GENERIC: return g_opt_generic.load();
     case KLAB_OPT_CTAS_PER_SM: return g_opt_ctas_per_sm.load();
     default: return KLAB_E_INVALID;

@@ -75,9 +75,8 @@ template <int F, int X>
 cudaError_t run_fx(const GemvParams& p, const LaunchShape& s, cudaStream_t stream, int* occ) {
   if (s.xmode == XM_SMEM) return run_mt<F, X, XM_SMEM>(p, s, stream, occ);
   if (s.xmode == XM_GLOBAL) return run_mt<F, X, XM_GLOBAL>(p, s, stream, occ);
-  // 16-bit x staging exists for the 16-bit-weight formats only.
-  if constexpr (X != X_F32 && (F == W_BF16 || F == W_F16 || F == W_CBF16))
-    return run_mt<F, X, XM_SMEM16>(p, s, stream, occ);
+  // 16-bit x staging exists for every 16-bit x.
+  if constexpr (X != X_F32) return run_mt<F, X, XM_SMEM16>(p, s, stream, occ);
   return cudaErrorNotSupported;
 }
 

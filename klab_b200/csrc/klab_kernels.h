@@ -5,6 +5,9 @@
 #include "../../include/klab_b200.h"
 
 namespace klab {
+// Tensor-core projection for token tiles (kind 0: BF16 weights, 1: INT8 + per-row scale).
+int tc_gemm_launch(int kind, const void* x, int ldx, const void* w, const float* scales, void* out, int ldo,
+                   int out_f32, int m, int n, int k, int* status, cudaStream_t stream);
 // Device address of the status word on the current device (nullptr on error).
 int* device_status_address();
 cudaError_t launch_cbf16_unpack(const void* payload, const unsigned* metadata, void* out, int n, int k,
