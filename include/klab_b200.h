@@ -83,6 +83,9 @@ extern "C" {
 #define KLAB_OPT_CTAS_PER_SM 3 /* cap on projection CTAs per SM (0, default: as many as fit) */
 #define KLAB_OPT_TENSOR 4      /* token tiles on tcgen05 tensor cores: 0 never, 1 (default) INT8 per-row
                                   weights at M >= 16, 2 INT8 per-row and BF16 weights at M >= 2 */
+#define KLAB_OPT_PROLOGUE 5    /* weight copies issued before the previous launch completes, per warp:
+                                  (items into shared memory) + 16 * (items prefetched into L2);
+                                  each part 0..3, -1 (default) the tuned choice */
 
 /* ---------------------------------------------------------------- projections */
 

@@ -32,6 +32,9 @@ std::atomic<int> g_opt_pdl{1};
 std::atomic<int> g_opt_split{-1};
 std::atomic<int> g_opt_generic{0};
 std::atomic<int> g_opt_ctas_per_sm{0};  // 0: as many as fit
+// Prologue of the projection kernel: items copied into shared memory (low 4 bits)
+// and items prefetched into L2 (next 4 bits) before griddepcontrol.wait; -1: tuned.
+std::atomic<int> g_opt_prologue{-1};
 // Tensor-core path for token tiles: 0 off; 1 (default) INT8 per-row weights at
 // M >= 16, where the tile is a dense contraction; 2 INT8 per-row and BF16 weights
 // at M >= 2 (BF16 M-tiles then differ from M = 1 in the last bits; the
@@ -343,6 +346,11 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   p.out_f32 = out_dt == KLAB_DT_F32;
   p.chunks = chunks;
   p.use_tma = tma;
+  {
+    const int pro = g_opt_prologue.load();
+    p.pro_smem = pro < 0 ? kProSmem : (pro & 15);
+    p.pro_l2 = pro < 0 ? kProL2 : (pro >> 4);
+  }
 
   const size_t need = workspace_need(tiles, mt, n, chunks);
   const bool can_split = ws && ws_bytes >= need && chunks >= 2 && aligned16(ws) &&
@@ -664,6 +672,10 @@ int klab_set_option(int option, int value) {
       if (value < 0 || value > 2) return KLAB_E_INVALID;
       g_opt_tensor.store(value);
       return 0;
+    case KLAB_OPT_PROLOGUE:
+      if (value != -1 && (value < 0 || (value & 15) > 3 || (value >> 4) > 3)) return KLAB_E_INVALID;
+      g_opt_prologue.store(value);
+      return 0;
     default: return KLAB_E_INVALID;
   }
 }
@@ -675,6 +687,7 @@ int klab_get_option(int option) {
     case KLAB_OPT_TENSOR: return g_opt_tensor.load();
     case KLAB_OPT_GENERIC: return g_opt_generic.load();
     case KLAB_OPT_CTAS_PER_SM: return g_opt_ctas_per_sm.load();
+    case KLAB_OPT_PROLOGUE: return g_opt_prologue.load();
     default: return KLAB_E_INVALID;
   }
 }

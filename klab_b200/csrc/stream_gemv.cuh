@@ -81,8 +81,20 @@ constexpr int kDepth = KLAB_DEPTH;    // ring slots per warp
 constexpr int kSegUnroll = KLAB_SEG_UNROLL;
 constexpr int kSegs = 8;              // segments per chunk
 constexpr int kWeightSlot = 4096;     // weight bytes per full chunk
-constexpr int kMetaRing = 2 * kDepth - 1;  // coded: metadata entries per warp
+constexpr int kMetaRing = 2 * kDepth;  // coded: metadata entries per warp
 constexpr int kMetaEntry = 128;       // 32 blocks * 4 bytes
+// Default prologue (before griddepcontrol.wait), per warp: items copied into the
+// ring and the following items prefetched into L2. x is staged right after the
+// wait and its loads queue behind this SM's bulk copies, so copies into shared
+// memory delay x; L2 prefetches only load the weights into L2.
+#ifndef KLAB_PRO_SMEM
+#define KLAB_PRO_SMEM 1
+#endif
+#ifndef KLAB_PRO_L2
+#define KLAB_PRO_L2 0
+#endif
+constexpr int kProSmem = KLAB_PRO_SMEM;
+constexpr int kProL2 = KLAB_PRO_L2;
 
 template <int F>
 struct WTraits;
@@ -185,6 +197,8 @@ struct GemvParams {
   int split;      // 0: rows dealt to CTAs; 1: items dealt to CTAs (split-K)
   int use_tma;    // 1: bulk copies; 0: cooperative loads (any alignment)
   int chunks;     // S = ceil(K / KC)
+  int pro_smem;   // prologue: items copied into the ring before griddepcontrol.wait
+  int pro_l2;     // prologue: following items prefetched into L2 (uncoded formats)
 };
 
 // Segment of a launch row and the row's index inside that segment.
@@ -235,14 +249,180 @@ struct XLayout {
   static constexpr int SEG_BYTES = NV * 512;            // one segment of one token
 };
 
+// FP16 activations for integer and E2M1 weights. Their weight values are exact in
+// FP16 (|int8| <= 127, E2M1 magnitudes 0..6), so with x in FP16 every product is
+// one fma.rn.f32.f16 on unconverted 16-bit operands: exact product, one rounding,
+// the same value sequence and accumulators as the FP32 path, so the same bits.
+// BF16 x is staged as FP16 after multiplying token t by 2^s_t (exact), chosen
+// per token from the exponents of its nonzero values; the row total is multiplied
+// by 2^-s_t (exact) before any weight scale. The scaling commutes with every
+// rounding when the token's values satisfy (bf16 exponent fields, nonzero values)
+//   emin >= 39       products, group sums and group-scaled sums stay normal in
+//                    FP32 (group scales are FP16 or E4M3, >= 2^-24),
+//   emax <= 200      no FP32 overflow in either scaling,
+//   emax - emin <= 32  every scaled value is exact in FP16 (largest < 2^16,
+//                    lowest set bit >= 2^-24), with s_t = 142 - emax;
+// otherwise the tile keeps BF16 staging and the FP32 path. FP16 x needs no check.
+template <int F, int X, int XM>
+struct HalfX {
+  static constexpr bool value = XM == XM_SMEM16 && (X == X_BF16 || X == X_F16) &&
+                                (F == W_I8_ROW || F == W_FP4_G32H || F == W_FP4_G16E);
+};
+
+// Per-CTA state of the FP16 staging (shared memory).
+struct XHalfState {
+  int emax[8], emin[8];  // per token: bf16 exponent field range of the nonzero values
+  float inv[8];          // per token: 2^-s_t
+  int on;                // 1: x is staged as FP16
+};
+
+// Exponent field range of the nonzero BF16 values in four words (eight values).
+__device__ __forceinline__ void bf16_exp_range(const uint4 v, int& emax, int& emin) {
+  const unsigned w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const unsigned b = (w[i] >> (16 * h)) & 0xffffu;
+      const int e = static_cast<int>((b >> 7) & 0xffu);
+      emax = max(emax, e);
+      emin = min(emin, (b & 0x7fffu) ? e : 255);
+    }
+  }
+}
+
+// Eight BF16 values times 2^s (exact by the staging rule) as eight FP16 values.
+__device__ __forceinline__ uint4 bf16x8_to_f16x8_scaled(const uint4 v, float scale) {
+  const unsigned w[4] = {v.x, v.y, v.z, v.w};
+  unsigned o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = mul_rn(__uint_as_float(w[i] << 16), scale);
+    const float hi = mul_rn(__uint_as_float(w[i] & 0xffff0000u), scale);
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(o[i]) : "f"(hi), "f"(lo));
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 template <int F, int X, int XM, int MT>
-__device__ void stage_x(const GemvParams& p, int tile, unsigned char* xs, int segs) {
+__device__ void stage_x(const GemvParams& p, int tile, unsigned char* xs, int segs, XHalfState* xh) {
+  constexpr bool HALF = HalfX<F, X, XM>::value;
   constexpr int VALS = WTraits<F>::VALS;
   constexpr int EB = XLayout<F, XM>::EB;
   constexpr int PER = 16 / EB;  // values per 16-byte unit
   constexpr int NV = XLayout<F, XM>::NV;
   const int kpad = segs * 32 * VALS;
   const int units = MT * kpad / PER;
+  const int upt = kpad / PER;  // units per token
+  // Aligned rows: one 16-byte (or 8-byte for 16-bit x staged as FP32) L2 load per
+  // unit, a batch of them in flight per thread before the first store. Every CTA
+  // reads the same few lines, so per-element loads would multiply the L2 requests
+  // on them by the vector width; this staging sits on every launch's critical path.
+  constexpr int XBYTES = (X == X_F32) ? 4 : 2;
+  constexpr int LBYTES = PER * XBYTES;  // global bytes per unit: 16 or 8
+  static_assert(LBYTES == 16 || LBYTES == 8, "16-bit staging takes 16-bit x only");
+  if ((p.k % PER) == 0 && (p.ldx % PER) == 0 && (reinterpret_cast<uintptr_t>(p.x) % LBYTES) == 0) {
+    constexpr int B = 4;
+    for (int u0 = threadIdx.x; u0 < units; u0 += B * blockDim.x) {
+      uint4 v[B];
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int u = u0 + b * blockDim.x;
+        v[b] = make_uint4(0u, 0u, 0u, 0u);
+        if (u < units) {
+          const int t = u / upt;
+          const int col0 = (u - t * upt) * PER;
+          const int token = tile * MT + t;
+          if (token < p.m && col0 < p.k) {
+            const char* src = static_cast<const char*>(p.x) +
+                              (static_cast<long long>(token) * p.ldx + col0) * XBYTES;
+            if constexpr (LBYTES == 16) {
+              v[b] = __ldcg(reinterpret_cast<const uint4*>(src));
+            } else {
+              const uint2 h = __ldcg(reinterpret_cast<const uint2*>(src));
+              v[b] = make_uint4(h.x, h.y, 0u, 0u);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < B; ++b) {
+        const int u = u0 + b * blockDim.x;
+        if (u >= units) break;
+        const int t = u / upt;
+        const int col0 = (u - t * upt) * PER;
+        const int g = col0 / (32 * VALS);
+        const int r = col0 - g * 32 * VALS;
+        const int l = r / VALS;
+        const int i = (r - l * VALS) / PER;
+        unsigned char* dst = xs + ((((t * segs + g) * NV + i) * 32 + l) << 4);
+        uint4 s = v[b];
+        if constexpr (HALF && X == X_BF16) {
+          // Units of one batch step of a warp belong to one token (units per
+          // token is a multiple of 32), so the warp reduces before one atomic.
+          int emax = 0, emin = 255;
+          bf16_exp_range(v[b], emax, emin);
+          emax = __reduce_max_sync(0xffffffffu, emax);
+          emin = __reduce_min_sync(0xffffffffu, emin);
+          if ((threadIdx.x & 31) == 0) {
+            atomicMax(&xh->emax[t], emax);
+            atomicMin(&xh->emin[t], emin);
+          }
+        }
+        if constexpr (EB == 4 && X != X_F32) {
+          // Four 16-bit values widened to FP32.
+          const unsigned lo = v[b].x, hi = v[b].y;
+          if constexpr (X == X_BF16)
+            s = make_uint4(lo << 16, lo & 0xffff0000u, hi << 16, hi & 0xffff0000u);
+          else
+            s = make_uint4(__float_as_uint(f16lo(lo)), __float_as_uint(f16hi(lo)), __float_as_uint(f16lo(hi)),
+                           __float_as_uint(f16hi(hi)));
+        }
+        *reinterpret_cast<uint4*>(dst) = s;
+      }
+    }
+    if constexpr (HALF && X == X_BF16) {
+      __syncthreads();
+      bool fast = true;
+#pragma unroll
+      for (int t = 0; t < MT; ++t) {
+        const int emax = xh->emax[t], emin = xh->emin[t];
+        fast = fast && (emin == 255 || (emax <= 200 && emin >= 39 && emax - emin <= 32));
+      }
+      if (fast) {
+        for (int u = threadIdx.x; u < units; u += blockDim.x) {
+          const int t = u / upt;
+          const int col0 = (u - t * upt) * PER;
+          const int g = col0 / (32 * VALS);
+          const int r = col0 - g * 32 * VALS;
+          const int l = r / VALS;
+          const int i = (r - l * VALS) / PER;
+          uint4* dst = reinterpret_cast<uint4*>(xs + ((((t * segs + g) * NV + i) * 32 + l) << 4));
+          const float scale = xh->emin[t] == 255 ? 1.0f : __int_as_float((269 - xh->emax[t]) << 23);  // 2^s_t
+          *dst = bf16x8_to_f16x8_scaled(*dst, scale);
+        }
+      }
+      if (threadIdx.x == 0) {
+        xh->on = fast ? 1 : 0;
+        for (int t = 0; t < MT; ++t)  // 2^-s_t
+          xh->inv[t] = (!fast || xh->emin[t] == 255) ? 1.0f : __int_as_float((xh->emax[t] - 15) << 23);
+      }
+    } else if constexpr (HALF) {
+      if (threadIdx.x == 0) {
+        xh->on = 1;
+        for (int t = 0; t < MT; ++t) xh->inv[t] = 1.0f;
+      }
+    }
+    return;
+  }
+  if constexpr (HALF) {
+    // Unaligned rows keep the staged 16-bit values as they are: FP16 x runs the
+    // FP16 path unscaled, BF16 x the FP32 path.
+    if (threadIdx.x == 0) {
+      xh->on = (X == X_F16) ? 1 : 0;
+      for (int t = 0; t < MT; ++t) xh->inv[t] = 1.0f;
+    }
+  }
   for (int u = threadIdx.x; u < units; u += blockDim.x) {
     const int t = u / (kpad / PER);
     const int col0 = (u - t * (kpad / PER)) * PER;  // first column of this unit
@@ -551,6 +731,98 @@ __device__ __forceinline__ void compute_item(unsigned slot, unsigned meta_entry,
   for (int t = 0; t < MT; ++t) P[t] = warp_allsum(SCALED ? acc[t] : acc8[t].tree());
 }
 
+// Four signed int8 codes (one word) -> two FP16 pairs, exactly: bytes biased by
+// 128 become the low mantissa byte of 1024 + u, and 1152 is subtracted in FP16.
+__device__ __forceinline__ void int8x4_to_f16x4(unsigned q, unsigned& h01, unsigned& h23) {
+  const unsigned u = q ^ 0x80808080u;
+  const unsigned a = __byte_perm(u, 0x64646464u, 0x4140u), b = __byte_perm(u, 0x64646464u, 0x4342u);
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h01) : "r"(a), "r"(0x64806480u));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(h23) : "r"(b), "r"(0x64806480u));
+}
+
+// compute_item for HalfX formats with x staged as FP16: the same values, sums and
+// order as compute_item, each product a mixed fma.rn.f32.f16 on the raw pairs.
+template <int F, int MT, bool FULL>
+__device__ __forceinline__ void compute_item_h(unsigned slot, int lane, int L, unsigned xs_lane, int tok_stride,
+                                               float (&P)[MT]) {
+  constexpr int VALS = WTraits<F>::VALS;
+  constexpr bool SCALED = (F == W_FP4_G32H || F == W_FP4_G16E);
+  constexpr int SEG = XLayout<F, XM_SMEM16>::SEG_BYTES;
+  constexpr int WORDS = VALS / 2;  // FP16 pairs per lane and segment
+  Acc8 acc8[MT];
+  float acc[MT];
+#pragma unroll
+  for (int t = 0; t < MT; ++t) {
+    acc8[t].zero();
+    acc[t] = 0.0f;
+  }
+  constexpr int UNROLL = MT <= 2 ? kSegUnroll : (kSegUnroll < 2 ? kSegUnroll : 2);
+#pragma unroll(UNROLL)
+  for (int j = 0; j < kSegs; ++j) {
+    if (!FULL) {
+      if (32 * VALS * j >= L) break;
+      if ((32 * j + lane) * VALS >= L) continue;
+    }
+    const unsigned xs_seg = xs_lane + j * SEG;
+    const uint4 wv = lds128(slot + (j * 32 + lane) * 16);
+    const unsigned q[4] = {wv.x, wv.y, wv.z, wv.w};
+    unsigned wh[WORDS];  // pair i: values 2i, 2i + 1
+    if constexpr (F == W_I8_ROW) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) int8x4_to_f16x4(q[i], wh[2 * i], wh[2 * i + 1]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) wh[4 * i + b] = e2m1x2_to_f16x2((q[i] >> (8 * b)) & 0xffu);
+    }
+    float s0 = 1.0f, s1 = 1.0f;
+    if constexpr (F == W_FP4_G32H) {
+      s0 = f16_to_f32(lds16(slot + kWeightSlot + 2 * (32 * j + lane)));
+    } else if constexpr (F == W_FP4_G16E) {
+      const unsigned h = e4m3x2_to_f16x2(lds16(slot + kWeightSlot + 64 * j + 2 * lane));
+      s0 = f16lo(h);
+      s1 = f16hi(h);
+    }
+#pragma unroll
+    for (int t = 0; t < MT; ++t) {
+      unsigned xq[WORDS];
+#pragma unroll
+      for (int i = 0; i < WORDS / 4; ++i) {
+        const uint4 v = lds128(xs_seg + t * tok_stride + i * 512);
+        xq[4 * i] = v.x;
+        xq[4 * i + 1] = v.y;
+        xq[4 * i + 2] = v.z;
+        xq[4 * i + 3] = v.w;
+      }
+      if constexpr (!SCALED) {
+#pragma unroll
+        for (int i = 0; i < WORDS; ++i) {
+          f2& a = acc8[t].a[i & 3];
+          a.x = fma_half_mixed<false, true>(xq[i], wh[i], a.x);
+          a.y = fma_half_mixed<true, true>(xq[i], wh[i], a.y);
+        }
+      } else {
+        constexpr int GW = ((F == W_FP4_G16E) ? 16 : VALS) / 2;  // pairs per scale group
+#pragma unroll
+        for (int g0 = 0; g0 < WORDS; g0 += GW) {
+          Acc8 sub;
+          sub.zero();
+#pragma unroll
+          for (int i = g0; i < g0 + GW; ++i) {
+            f2& a = sub.a[i & 3];
+            a.x = fma_half_mixed<false, true>(xq[i], wh[i], a.x);
+            a.y = fma_half_mixed<true, true>(xq[i], wh[i], a.y);
+          }
+          acc[t] = fma_rn(sub.tree(), g0 == 0 ? s0 : s1, acc[t]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < MT; ++t) P[t] = warp_allsum(SCALED ? acc[t] : acc8[t].tree());
+}
+
 // ------------------------------------------------------------------ filling
 
 template <int F>
@@ -728,6 +1000,17 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
     bulk_g2s(slot, src, bytes, bar);
     if (sbytes) bulk_g2s(slot + kWeightSlot, ssrc, sbytes, bar);
   };
+  // lane 0: L2 prefetch of the item at cursor it (uncoded formats).
+  auto prefetch_item = [&](const Cursor& it) {
+    const int L = min(KC, k - it.c * KC);
+    const RowRef r = resolve_row(p, it.row);
+    const char* ssrc = nullptr;
+    int sbytes = 0;
+    bulk_prefetch_l2(r.w + w_offset_bytes<F>(static_cast<long long>(r.local) * k + it.c * KC),
+                     static_cast<unsigned>(w_offset_bytes<F>(L)));
+    scale_span<F>(r, k, it.c, L, &ssrc, &sbytes);
+    if (sbytes) bulk_prefetch_l2(ssrc, static_cast<unsigned>(sbytes));
+  };
 
   bool ok = true;
   int issued_meta = 0, issued = 0;  // lane 0 bookkeeping
@@ -737,15 +1020,17 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
       fence_mbar_init();
     }
     __syncwarp();
-    // Prologue: weights do not depend on the previous grid, so these copies are
-    // in flight before griddepcontrol.wait.
+    // Prologue: weights do not depend on the previous grid, so the first items
+    // are copied (or prefetched into L2) before griddepcontrol.wait and stream
+    // while the previous grid drains.
+    const int pro = min(min(p.pro_smem, kDepth), nitems);
     if (lane == 0) {
       if constexpr (CODED) {
         for (; issued_meta < min(kMetaRing, nitems); ++issued_meta) {
           issue_meta(issued_meta, mcur);
           mcur.advance(S, row_step);
         }
-        for (; issued < min(kDepth - 1, nitems); ++issued) {
+        for (; issued < pro; ++issued) {
           if (!mbar_wait(mbar0 + (issued % kMetaRing) * 8, (issued / kMetaRing) & 1)) {
             ok = false;
             break;
@@ -754,9 +1039,14 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
           iss.advance(S, row_step);
         }
       } else {
-        for (; issued < min(kDepth - 1, nitems); ++issued) {
+        for (; issued < pro; ++issued) {
           issue_item(issued, iss);
           iss.advance(S, row_step);
+        }
+        Cursor pc = iss;
+        for (int i = issued; i < min(issued + p.pro_l2, nitems); ++i) {
+          prefetch_item(pc);
+          pc.advance(S, row_step);
         }
       }
     }
@@ -770,10 +1060,33 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
     if (!wait_flag_geq(p.gather.wait_flags + p.gather.wait_slot * p.gather.npeers + threadIdx.x, target))
       record_status(p.status, kStatusFlagTimeout);
   }
+  __shared__ XHalfState s_xh;
+  if (threadIdx.x < 8) {
+    s_xh.emax[threadIdx.x] = 0;
+    s_xh.emin[threadIdx.x] = 255;
+  }
   __syncthreads();
-  if constexpr (XM != XM_GLOBAL) stage_x<F, X, XM, MT>(p, tile, xs, segs);
+  if constexpr (XM != XM_GLOBAL) stage_x<F, X, XM, MT>(p, tile, xs, segs, &s_xh);
   __syncthreads();
+  constexpr bool HALF = HalfX<F, X, XM>::value;
+  const bool xhalf = HALF && s_xh.on;
   grid_launch_dependents();
+  if (p.use_tma && ok) {
+    // Fill the rest of the ring; afterwards each consumed slot is refilled at once.
+    if (lane == 0) {
+      for (; issued < min(kDepth, nitems); ++issued) {
+        if constexpr (CODED) {
+          if (!mbar_wait(mbar0 + (issued % kMetaRing) * 8, (issued / kMetaRing) & 1)) {
+            ok = false;
+            break;
+          }
+        }
+        issue_item(issued, iss);
+        iss.advance(S, row_step);
+      }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+  }
 
   constexpr int SEG = XLayout<F, XM>::SEG_BYTES;
   const int tok_stride = segs * SEG;
@@ -799,19 +1112,6 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
     const unsigned slot = slot0 + (q % kDepth) * SLOT;
     const unsigned entry = meta0 + (q % kMetaRing) * kMetaEntry;
     if (p.use_tma) {
-      if (lane == 0 && issued < nitems && issued == q + kDepth - 1) {
-        bool ready = true;
-        if constexpr (CODED) ready = mbar_wait(mbar0 + (issued % kMetaRing) * 8, (issued / kMetaRing) & 1);
-        if (ready) {
-          issue_item(issued, iss);
-          iss.advance(S, row_step);
-          ++issued;
-        } else {
-          ok = false;
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
       const bool landed = mbar_wait(pbar0 + (q % kDepth) * 8, (q / kDepth) & 1);
       if (!__all_sync(0xffffffffu, landed)) {
         ok = false;
@@ -857,13 +1157,37 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
     const unsigned xs_lane = xs_lane0 + c * kSegs * SEG;
     const char* xg = xg_lane0 + static_cast<long long>(c) * KC * XB;
     float P[MT];
-    if (L == KC)
+    if (HALF && xhalf) {
+      if constexpr (HALF) {
+        if (L == KC)
+          compute_item_h<F, MT, true>(slot, lane, L, xs_lane, tok_stride, P);
+        else
+          compute_item_h<F, MT, false>(slot, lane, L, xs_lane, tok_stride, P);
+      }
+    } else if (L == KC) {
       compute_item<F, X, XM, MT, true>(slot, entry, first_unit, lane, L, xs_lane, tok_stride, xg, xg_stride, tvalid,
                                        P);
-    else
+    } else {
       compute_item<F, X, XM, MT, false>(slot, entry, first_unit, lane, L, xs_lane, tok_stride, xg, xg_stride,
                                         tvalid, P);
+    }
     __syncwarp();  // every lane is done with this slot before it is refilled
+    if (p.use_tma) {
+      // Refill the slot just consumed with item q + kDepth (its metadata was
+      // requested two items ago).
+      if (lane == 0 && issued < nitems) {
+        bool ready = true;
+        if constexpr (CODED) ready = mbar_wait(mbar0 + (issued % kMetaRing) * 8, (issued / kMetaRing) & 1);
+        if (ready) {
+          issue_item(issued, iss);
+          iss.advance(S, row_step);
+          ++issued;
+        } else {
+          ok = false;
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
 
     if (row_complete) {
 #pragma unroll
@@ -872,7 +1196,8 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
 #pragma unroll
         for (int t = 0; t < MT; ++t) {
           const int token = tile * MT + t;
-          if (lane == t && token < p.m) finalize_token<F, MT>(p, rref, token, rowsum[t], row_scale);
+          if (lane == t && token < p.m)
+            finalize_token<F, MT>(p, rref, token, xhalf ? mul_rn(rowsum[t], s_xh.inv[t]) : rowsum[t], row_scale);
         }
       }
     } else {
@@ -902,7 +1227,7 @@ __global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(cons
               const float* src = p.ws + ((static_cast<long long>(tile) * MT + t) * n + row) * S;
               float total = __ldcg(src);
               for (int cc = 1; cc < S; ++cc) total = add_rn(total, __ldcg(src + cc));
-              finalize_token<F, MT>(p, rref, token, total, row_scale);
+              finalize_token<F, MT>(p, rref, token, xhalf ? mul_rn(total, s_xh.inv[t]) : total, row_scale);
             }
           }
           if (lane == 0) *ticket = 0u;
