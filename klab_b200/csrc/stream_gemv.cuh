@@ -67,7 +67,10 @@ enum XMode : int { XM_SMEM = 0, XM_GLOBAL = 1, XM_SMEM16 = 2 };
 #define KLAB_WARPS 16      // warps per CTA for single-token tiles
 #endif
 #ifndef KLAB_WARPS_MT
-#define KLAB_WARPS_MT 8    // warps per CTA for multi-token tiles (register budget)
+#define KLAB_WARPS_MT 16   // warps per CTA for 2- and 4-token tiles
+#endif
+#ifndef KLAB_WARPS_MT8
+#define KLAB_WARPS_MT8 8   // warps per CTA for 8-token tiles (their x takes the shared memory)
 #endif
 #ifndef KLAB_DEPTH
 #define KLAB_DEPTH 2
@@ -76,7 +79,9 @@ enum XMode : int { XM_SMEM = 0, XM_GLOBAL = 1, XM_SMEM16 = 2 };
 #define KLAB_SEG_UNROLL 8
 #endif
 // Warps per CTA for a token tile of MT.
-__host__ __device__ constexpr int warps_for(int mt) { return mt == 1 ? KLAB_WARPS : KLAB_WARPS_MT; }
+__host__ __device__ constexpr int warps_for(int mt) {
+  return mt == 1 ? KLAB_WARPS : mt == 8 ? KLAB_WARPS_MT8 : KLAB_WARPS_MT;
+}
 constexpr int kDepth = KLAB_DEPTH;    // ring slots per warp
 constexpr int kSegUnroll = KLAB_SEG_UNROLL;
 constexpr int kSegs = 8;              // segments per chunk
@@ -590,6 +595,38 @@ __device__ __forceinline__ void load_w(unsigned slot, unsigned meta_entry, unsig
   }
 }
 
+// Two codec-v1 codes, the low one in bits 0-11 and the high one in bits 16-27
+// (bits 12-15 and 28-31 ignored) -> two BF16 values, exactly the upper halves of
+// cbf16_code's FP32 bits; base2 holds the block's exponent base at BF16 bits 7-14
+// of both halves.
+__device__ __forceinline__ unsigned cbf16_pair(unsigned p, unsigned base2) {
+  return (p & 0x007f007fu) | ((p << 8) & 0x80008000u) | (base2 + ((p >> 1) & 0x07800780u));
+}
+
+// The lane's eight 16-bit weights of segment j as four pairs (value 2i in the low
+// half of word i): raw 16-bit formats read them, coded BF16 decodes a coded block
+// two codes at a time.
+template <int F>
+__device__ __forceinline__ uint4 load_w16(unsigned slot, unsigned meta_entry, unsigned first_unit, int j, int lane) {
+  if constexpr (F == W_CBF16) {
+    const int block = 4 * j + (lane >> 3);
+    const int q8 = lane & 7;
+    const unsigned meta = lds32(meta_entry + 4 * block);
+    const unsigned off = slot + (((meta & 0x7fffffu) - first_unit) << 5);
+    if (meta >> 31) return lds128(off + 16 * q8);
+    const unsigned a = lds32(off + 12 * q8), b = lds32(off + 12 * q8 + 4), c = lds32(off + 12 * q8 + 8);
+    const unsigned base2 = ((meta & 0x7f800000u) >> 16) * 0x00010001u;
+    const unsigned p01 = __byte_perm(a, a << 4, 0x7610u);
+    const unsigned p23 = __byte_perm(__funnelshift_r(a, b, 24), b << 12, 0x7610u);
+    const unsigned p45 = __byte_perm(b >> 16, __funnelshift_r(b, c, 12), 0x7610u);
+    const unsigned p67 = __byte_perm(c >> 8, c >> 4, 0x7610u);
+    return make_uint4(cbf16_pair(p01, base2), cbf16_pair(p23, base2), cbf16_pair(p45, base2),
+                      cbf16_pair(p67, base2));
+  } else {
+    return lds128(slot + (j * 32 + lane) * 16);
+  }
+}
+
 // ------------------------------------------------------------------ item math
 
 #ifndef KLAB_MIXED_BF16
@@ -623,7 +660,7 @@ __device__ __forceinline__ float fma_half_mixed(unsigned x2, unsigned w2, float 
 // True when a (weight format, x mode) pair multiplies 16-bit operands directly.
 template <int F, int XM>
 struct MixedPath {
-  static constexpr bool value = KLAB_MIXED_BF16 && (F == W_BF16 || F == W_F16) && XM == XM_SMEM16;
+  static constexpr bool value = KLAB_MIXED_BF16 && (F == W_BF16 || F == W_F16 || F == W_CBF16) && XM == XM_SMEM16;
 };
 
 // Lane accumulators of one token: eight FP32 sums held as four pairs. Value v
@@ -673,7 +710,7 @@ __device__ __forceinline__ void compute_item(unsigned slot, unsigned meta_entry,
     const unsigned xs_seg = xs_lane + j * SEG;
     const char* xg_seg = xg + static_cast<long long>(32 * VALS * j) * XB;
     if constexpr (MIXED) {
-      const uint4 wv = lds128(slot + (j * 32 + lane) * 16);
+      const uint4 wv = load_w16<F>(slot, meta_entry, first_unit, j, lane);
       const unsigned wq[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
       for (int t = 0; t < MT; ++t) {
