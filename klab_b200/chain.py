@@ -261,8 +261,9 @@ class ProjectionChain:
     def trace_step(self, x):
         """Run one eager step of the persistent kernel with its timeline on and
         return it as an int64 tensor [stages, CTAs, slots] of global-timer ns
-        (slots: entered, previous stage done in this CTA, x staged, then each
-        warp's last item)."""
+        (slots: entered, previous stage done in this CTA, x staged, then per
+        warp: first item of the stage landed, run computed, done after its
+        deferred fold)."""
         if not self.persistent:
             raise ValueError("trace_step needs persistent=True")
         grid, slots = _native.chain_info(self._plan)

@@ -267,7 +267,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   // re-reading it from L1 for every item.
   const bool x16 = KLAB_PREFER_X16 && xdt != KLAB_DT_F32;
   for (;;) {
-    const int w_ = warps_for(mt);
+    const int w_ = warps_for(wfmt, mt);
     const size_t rings = bar_region_bytes(wfmt, w_) + static_cast<size_t>(w_) * warp_region_bytes(wfmt);
     const size_t cap = rings + kXSmemMin < kMaxSmem ? kMaxSmem - rings : kXSmemMin;
     if (x16 && static_cast<size_t>(mt) * kpad * 2 <= cap) {
@@ -294,7 +294,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   s.xmode = xmode;
   s.mt = mt;
   s.pdl = g_opt_pdl.load() != 0;
-  const int warps = warps_for(mt);
+  const int warps = warps_for(wfmt, mt);
   s.smem = bar_region_bytes(wfmt, warps) + warps * warp_region_bytes(wfmt) +
            (xmode == XM_SMEM ? static_cast<size_t>(mt) * kpad * 4
                              : xmode == XM_SMEM16 ? static_cast<size_t>(mt) * kpad * 2 : 0);
@@ -585,7 +585,7 @@ int klab_plan_info(void* plan_ptr, char* buffer, size_t bytes) {
   if (!plan || !buffer || bytes == 0) return KLAB_E_INVALID;
   const LaunchShape& s = plan->launch.s;
   const char* xmodes[] = {"smem_fp32", "global", "smem_16bit"};
-  const int warps = warps_for(s.mt);
+  const int warps = warps_for(plan->launch.wfmt, s.mt);
   const int len = std::snprintf(
       buffer, bytes,
       "{\"wfmt\": %d, \"xdtype\": %d, \"out_dtype\": %d, \"shape_mnk\": [%d, %d, %d], \"tile\": %d, "

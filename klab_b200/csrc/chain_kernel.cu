@@ -93,9 +93,11 @@ struct ChainParams {
 };
 
 // Trace slots per (stage, CTA): entered, every warp done with the previous
-// stage, x staged, then each warp's last item.
+// stage, x staged, then per warp: its first item of the stage landed, its run
+// computed, and done (after folding its deferred row).
 constexpr int kTraceCta = 3;
-constexpr int kTraceSlots = kTraceCta + kChainWarps;
+constexpr int kTraceWarp = 3;
+constexpr int kTraceSlots = kTraceCta + kTraceWarp * kChainWarps;
 
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
@@ -372,6 +374,7 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
         const bool landed = mbar_wait(bar, static_cast<unsigned>((g / kChainDepth) & 1));
         ok = __all_sync(0xffffffffu, landed);
         if (!ok) failed = g;
+        if (q == 0 && lane == 0) trace_mark(p, s, kTraceCta + kTraceWarp * warp);
       }
       if (ok) {
         const unsigned xs_lane = xs_lane0 + c * kSegs * 512;
@@ -401,8 +404,9 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
         ++row;
       }
     }
+    if (lane == 0) trace_mark(p, s, kTraceCta + kTraceWarp * warp + 1);
     if (deferred >= 0 && lane == 0) fold_split_row(p, st, deferred, tag, &s_broken);
-    if (lane == 0) trace_mark(p, s, kTraceCta + warp);
+    if (lane == 0) trace_mark(p, s, kTraceCta + kTraceWarp * warp + 2);
   }
 
   // CTA 0 publishes the step's output once every rank's last-stage words are in.

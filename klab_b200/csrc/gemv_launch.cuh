@@ -26,7 +26,7 @@ cudaError_t launch_one(const GemvParams& p, const LaunchShape& s, cudaStream_t s
   if (err != cudaSuccess) return err;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = s.grid;
-  cfg.blockDim = dim3(warps_for(MT) * 32, 1, 1);
+  cfg.blockDim = dim3(warps_for(F, MT) * 32, 1, 1);
   cfg.dynamicSmemBytes = s.smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -44,7 +44,7 @@ int occupancy_one(size_t smem) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, warps_for(MT) * 32, smem) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, warps_for(F, MT) * 32, smem) != cudaSuccess)
     return 0;
   return blocks;
 }

@@ -79,9 +79,17 @@ enum XMode : int { XM_SMEM = 0, XM_GLOBAL = 1, XM_SMEM16 = 2 };
 #define KLAB_SEG_UNROLL 8
 #endif
 // Warps per CTA for a token tile of MT.
-__host__ __device__ constexpr int warps_for(int mt) {
-  return mt == 1 ? KLAB_WARPS : mt == 8 ? KLAB_WARPS_MT8 : KLAB_WARPS_MT;
+// INT8 single-token tiles run as two 12-warp CTAs per SM: their item math is
+// the heaviest per byte, and 24 resident warps hide its latency better than 16
+// (config 2, M=1: 14.4 -> 13.3 us); the other formats keep one 16-warp CTA.
+#ifndef KLAB_WARPS_I8
+#define KLAB_WARPS_I8 12
+#endif
+__host__ __device__ constexpr bool int8_format(int f) { return f == W_I8_ROW || f == W_I8_G64; }
+__host__ __device__ constexpr int warps_for(int f, int mt) {
+  return mt == 1 ? (int8_format(f) ? KLAB_WARPS_I8 : KLAB_WARPS) : mt == 8 ? KLAB_WARPS_MT8 : KLAB_WARPS_MT;
 }
+__host__ __device__ constexpr int min_blocks_for(int f, int mt) { return mt == 1 && int8_format(f) ? 2 : 1; }
 constexpr int kDepth = KLAB_DEPTH;    // ring slots per warp
 constexpr int kSegUnroll = KLAB_SEG_UNROLL;
 constexpr int kSegs = 8;              // segments per chunk
@@ -951,11 +959,12 @@ __device__ __forceinline__ void finalize_token(const GemvParams& p, const RowRef
   }
 }
 
-// Grid (G, ceil(M / MT)); block warps_for(MT)*32. Dynamic shared memory:
+// Grid (G, ceil(M / MT)); block warps_for(F, MT)*32. Dynamic shared memory:
 // [mbarriers][kWarps warp regions: kDepth slots (+ metadata ring)][x staging].
 template <int F, int X, int XM, int MT>
-__global__ void __launch_bounds__(warps_for(MT) * 32, 1) stream_gemv_kernel(const GemvParams p) {
-  constexpr int kWarps = warps_for(MT);
+__global__ void __launch_bounds__(warps_for(F, MT) * 32, min_blocks_for(F, MT))
+    stream_gemv_kernel(const GemvParams p) {
+  constexpr int kWarps = warps_for(F, MT);
   constexpr int KC = Layout<F>::KC;
   constexpr int SLOT = Layout<F>::SLOT;
   constexpr int VALS = WTraits<F>::VALS;

@@ -483,3 +483,29 @@ def test_persistent_chain_equals_launch_chain(native, dims):
     assert int(pc.epoch.item()) == 2 + 1 + 3  # eager steps, capture warm-up, replays
     assert native.device_status() == 0
     pc.release()
+
+
+def test_persistent_chain_timeline(native):
+    """trace_step returns ordered global-timer stamps for every stage and CTA
+    (entered <= previous stage done <= x staged; per warp staged <= first item
+    landed <= run computed <= done) and leaves the step's result unchanged."""
+    from klab_b200.chain import ChainShape, ProjectionChain
+
+    shape = ChainShape(layers=2, hidden=1024, kv=256, ffn=3584)
+    x = dev_bf16(og.normal_bf16_bits(71, (1, 1024), 1.0))
+    pc = ProjectionChain(shape, seed=4, persistent=True)
+    ref = pc.forward_eager(x).clone()
+    tr = pc.trace_step(x).numpy()
+    assert same_bits(pc.forward_eager(x), ref)
+    stages, grid, slots = tr.shape
+    assert stages == 4 * shape.layers and slots == 3 + 3 * 16
+    assert (tr[:, :, :3] > 0).all()
+    assert (tr[:, :, 0] <= tr[:, :, 1]).all() and (tr[:, :, 1] <= tr[:, :, 2]).all()
+    first, run, done = tr[:, :, 3::3], tr[:, :, 4::3], tr[:, :, 5::3]
+    staged = tr[:, :, 2:3]
+    assert (run >= staged).all() and (done >= run).all()
+    held = first > 0  # warps holding items of the stage
+    assert held.any(axis=2).all()
+    assert (first[held] >= np.broadcast_to(staged, first.shape)[held]).all() and (run[held] >= first[held]).all()
+    assert native.device_status() == 0
+    pc.release()
