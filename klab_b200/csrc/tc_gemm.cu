@@ -7,20 +7,26 @@
 // Warp roles (320 threads):
 //   warp 8      producer: 2-D TMA loads (cp.async.bulk.tensor, no multicast) of
 //               the next W tile [128 rows x 128 k] and x tile [16 x 128] per
-//               stage; BF16 W lands directly in the 128-byte-swizzled K-major
-//               layout the MMA reads (two 64-column atoms), INT8 W lands raw in a
-//               byte ring; lane 0 streams W and lane 1 streams x, each gated
-//               only by its own ring (x has a 6-stage ring released by its own
-//               commit, so its load latency never sits in the MMA loop);
+//               stage, all 128-byte swizzled; BF16 W lands directly in the
+//               K-major operand layout the MMA reads from shared memory (two
+//               64-column atoms), INT8 W lands raw in a 12-stage byte ring; lane
+//               0 streams W and lane 1 streams x, each gated only by its own ring
+//               (x has a 6-stage ring released by its own commit);
 //   warps 0..7  INT8 only: decode each raw tile to exact BF16 (|code| <= 127 has
-//               at most 7 significant bits) into the swizzled operand layout;
-//               warps 0..3 then run the epilogue: TMEM -> registers
+//               at most 7 significant bits) straight into tensor memory: warp w
+//               owns TMEM lanes 32*(w%4).. (its rows) and half w/4 of the stage's
+//               K, one row per thread, 64 codes -> 32 columns (tcgen05.st). The
+//               A operand then never occupies shared memory, which holds twice
+//               the raw ring instead (INT8 streaming is bound by bytes in
+//               flight). Warps 0..3 then run the epilogue: TMEM -> registers
 //               (tcgen05.ld), row scale, one RNE to BF16 (or FP32), store;
-//   warp 9      allocates 128 TMEM columns; lane 0 issues eight
-//               tcgen05.mma.kind::f16 (K = 16 each) per stage, MMA k into FP32
-//               accumulator k [128 lanes x 16 columns] (eight independent
-//               chains), and releases the stage's slots with tcgen05.commit; the
-//               epilogue adds the eight accumulators in a fixed tree.
+//   warp 9      allocates TMEM (128 accumulator columns, plus six 64-column A
+//               stages for INT8); lane 0 issues eight tcgen05.mma.kind::f16
+//               (K = 16 each) per stage, A from shared memory (BF16) or from
+//               tensor memory (INT8), MMA k into FP32 accumulator k [128 lanes x
+//               16 columns] (eight independent chains), and releases the stage's
+//               slots with tcgen05.commit; the epilogue adds the eight
+//               accumulators in a fixed tree.
 // Every mbarrier wait is bounded; on a timeout the kernel records the status
 // word, stops issuing, drains what it issued and frees TMEM.
 //
@@ -46,25 +52,32 @@ constexpr int kTcBK = 128;     // K per stage: two swizzle atoms
 #ifndef KLAB_TC_DECODERS
 #define KLAB_TC_DECODERS 8
 #endif
-constexpr int kTcDec = KLAB_TC_DECODERS;  // decoder warps (4, 8, 16 or 32)
+constexpr int kTcDec = KLAB_TC_DECODERS;  // decoder warps: two per TMEM lane quarter
+static_assert(kTcDec == 8 || kTcDec == 16, "INT8 decoders: warp w owns lane quarter w % 4 and K part w / 4");
+constexpr int kTcParts = kTcDec / 4;             // K parts of a stage per lane quarter
+constexpr int kTcChunks = 8 / kTcParts;          // 16-code chunks per decoder thread and stage
+constexpr int kTcDecCols = 8 * kTcChunks;        // TMEM columns a decoder thread writes per stage
 constexpr int kTcASub = kTcRows * kTcAtom * 2;   // 16 KiB per atom column
 constexpr int kTcBSub = kTcTok * kTcAtom * 2;    // 2 KiB per atom column
 constexpr int kTcABytes = 2 * kTcASub;           // 32 KiB: W operand of one stage
 constexpr int kTcBBytes = 2 * kTcBSub;           // 4 KiB: x operand of one stage
 constexpr int kTcRawBytes = kTcRows * kTcBK;     // 16 KiB: raw INT8 W of one stage
 constexpr int kTcX = 6;                          // x stages
-constexpr int kTcMaxA = 6, kTcMaxRaw = 6;
+constexpr int kTcMaxA = 6, kTcMaxRaw = 12;       // operand (BF16: smem; INT8: TMEM) and raw INT8 stages
 constexpr int kTcProducer = kTcDec, kTcMma = kTcDec + 1;  // warp indices
 constexpr int kTcThreads = 32 * (kTcDec + 2);
-// Shared memory, 1024-aligned: [W operand ring][x ring][raw ring][barriers, TMEM address].
-// BF16: 6 operand stages (TMA fills them directly), no raw ring; INT8: 3 operand
-// stages (filled by the decoders) and 6 raw stages.
-constexpr int kTcSmemData = kTcX * kTcBBytes + 6 * kTcABytes;      // the larger of the two layouts
-static_assert(3 * kTcABytes + 6 * kTcRawBytes <= 6 * kTcABytes, "INT8 layout fits the BF16 one");
+// Shared memory, 1024-aligned: BF16 [6 operand stages][x ring], INT8 [12 raw
+// stages][x ring]; then [barriers, TMEM address].
+constexpr int kTcSmemData = kTcX * kTcBBytes + 6 * kTcABytes;
+static_assert(kTcMaxRaw * kTcRawBytes == 6 * kTcABytes, "both layouts put the x ring at the same offset");
 constexpr int kTcBarBytes = 512;
 constexpr int kTcSmem = kTcSmemData + kTcBarBytes + 1024;  // + slack to align the base to 1024
 constexpr int kTcAcc = kTcBK / 16;                // independent accumulators (one per MMA of a stage)
-constexpr int kTcTmemCols = kTcAcc * kTcTok;      // 128 columns
+constexpr int kTcAccCols = kTcAcc * kTcTok;       // 128 accumulator columns
+constexpr int kTcACols = kTcBK / 2;               // 64 columns: one INT8 stage's A in TMEM (2 BF16 per column)
+// INT8: accumulators + six A stages = 512 columns (the whole TMEM of the SM; one CTA per SM).
+constexpr int kTcTmemColsI8 = kTcAccCols + kTcMaxA * kTcACols;
+static_assert(kTcTmemColsI8 == 512, "TMEM allocation must be a power of two");
 
 enum TcKind : int { TC_BF16 = 0, TC_I8_ROW = 1 };
 
@@ -114,6 +127,15 @@ __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t
       : "memory");
 }
 
+// A from tensor memory (K-major: row m in lane m, K pairs packed per column).
+__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(bdesc), "r"(kTcIdesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void tc_commit(unsigned bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -159,12 +181,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   __shared__ int s_fail;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bool int8 = p.kind == TC_I8_ROW;
-  const int DA = int8 ? 3 : kTcMaxA;          // W operand stages
+  const int DA = kTcMaxA;                     // W operand stages (BF16: shared memory; INT8: TMEM)
   const int DR = int8 ? kTcMaxRaw : 0;        // raw INT8 stages
   const unsigned base = smem_addr(smem);
-  const unsigned xoff = DA * kTcABytes, rawoff = xoff + kTcX * kTcBBytes;
+  const unsigned xoff = 6 * kTcABytes, rawoff = 0;  // raw INT8 ring where BF16 keeps its operand ring
   const unsigned bar0 = base + kTcSmemData;
-  // Barriers (8 bytes each): raw_full/empty[6], a_full/empty[6], x_full/empty[6], done; TMEM address.
+  const uint32_t tmem_cols = int8 ? kTcTmemColsI8 : kTcAccCols;
+  // Barriers (8 bytes each): raw_full/empty[12], a_full/empty[6], x_full/empty[6], done; TMEM address.
   const unsigned raw_full = bar0, raw_empty = bar0 + 8 * kTcMaxRaw;
   const unsigned a_full = bar0 + 16 * kTcMaxRaw, a_empty = a_full + 8 * kTcMaxA;
   const unsigned x_full = a_empty + 8 * kTcMaxA, x_empty = x_full + 8 * kTcX;
@@ -196,7 +219,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   }
   if (warp == kTcMma) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_addr(tmem_slot)), "r"(kTcTmemCols) : "memory");
+                 ::"r"(smem_addr(tmem_slot)), "r"(tmem_cols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
@@ -259,12 +282,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
         const unsigned abase = base + a * kTcABytes, bbase = base + xoff + xi * kTcBBytes;
         // MMA kk of every stage accumulates into its own TMEM accumulator, so the
         // eight MMAs of a stage are independent (one chain would serialise them).
+        // INT8: A stage a sits in TMEM columns kTcAccCols + 64a.., MMA kk reads 8 of them.
+        const uint32_t atmem = tmem + kTcAccCols + a * kTcACols;
 #pragma unroll
         for (int kk = 0; kk < kTcAcc; ++kk) {
           const unsigned off = 32 * (kk % 4);
           const int j = kk / 4;
-          tc_mma(tmem + kk * kTcTok, sw128_desc(abase + j * kTcASub + off), sw128_desc(bbase + j * kTcBSub + off),
-                 s > 0 ? 1u : 0u);
+          if (int8)
+            tc_mma_ts(tmem + kk * kTcTok, atmem + kk * 8, sw128_desc(bbase + j * kTcBSub + off), s > 0 ? 1u : 0u);
+          else
+            tc_mma(tmem + kk * kTcTok, sw128_desc(abase + j * kTcASub + off), sw128_desc(bbase + j * kTcBSub + off),
+                   s > 0 ? 1u : 0u);
         }
         tc_commit(a_empty + 8 * a);
         tc_commit(x_empty + 8 * xi);
@@ -289,28 +317,48 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
           }
           break;
         }
-        // Lane l of warp w: row 4*(w + kTcDec*it) + l/8, 16-byte chunk l%8 of the
-        // 128-byte raw row (a warp reads 512 consecutive bytes per step). Chunk c
-        // holds k = 16c..16c+15: atom column c/4, BF16 bytes 32*(c%4).. of its row.
-        const unsigned char* raw = smem + rawoff + r * kTcRawBytes;
-        unsigned char* dst = smem + a * kTcABytes;
+        tc_fence_after();  // the MMAs that read this TMEM stage have completed
+        // Thread = one row (TMEM lane 32*(w%4) + lane); warp w decodes K part
+        // w/4 of the stage: raw 16-byte chunks of its row (128-byte swizzled:
+        // chunk c of row r at (c ^ (r & 7)) * 16, conflict-free), each 16 codes
+        // -> 8 BF16 pairs = 8 TMEM columns.
+        const int quarter = warp & 3, part = warp >> 2;
+        const int row = 32 * quarter + lane;
+        const unsigned char* raw = smem + rawoff + r * kTcRawBytes + row * kTcBK;
+        unsigned v[32];
 #pragma unroll
-        for (int it = 0; it < kTcRows / (4 * kTcDec); ++it) {
-          const int row = 4 * (warp + kTcDec * it) + (lane >> 3);
-          const int c = lane & 7;
-          const uint4 q = *reinterpret_cast<const uint4*>(raw + row * kTcBK + 16 * c);
+        for (int j = 0; j < kTcChunks; ++j) {
+          const int c = kTcChunks * part + j;
+          const uint4 q = *reinterpret_cast<const uint4*>(raw + ((c ^ (row & 7)) << 4));
           uint4 lo, hi;
           int8x16_to_bf16(q, lo, hi);
-          unsigned char* sub = dst + (c >> 2) * kTcASub;
-          *reinterpret_cast<uint4*>(sub + sw128_offset(row, 2 * (c & 3))) = lo;
-          *reinterpret_cast<uint4*>(sub + sw128_offset(row, 2 * (c & 3) + 1)) = hi;
+          v[8 * j] = lo.x; v[8 * j + 1] = lo.y; v[8 * j + 2] = lo.z; v[8 * j + 3] = lo.w;
+          v[8 * j + 4] = hi.x; v[8 * j + 5] = hi.y; v[8 * j + 6] = hi.z; v[8 * j + 7] = hi.w;
         }
-        fence_proxy_async_smem();  // generic-proxy stores before the tensor core reads them
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(raw_empty + 8 * r);
-          mbar_arrive(a_full + 8 * a);
+        if (lane == 0) mbar_arrive(raw_empty + 8 * r);  // the raw slot is read
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(32 * quarter) << 16) + kTcAccCols + a * kTcACols +
+                               kTcDecCols * part;
+        if constexpr (kTcDecCols == 32) {
+          asm volatile(
+              "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+              "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+              ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+                "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]),
+                "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]),
+                "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+              : "memory");
+        } else {
+          asm volatile(
+              "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+              ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+                "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+              : "memory");
         }
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(a_full + 8 * a);
       }
     }
     // Epilogue (warps 0..3 own the TMEM lane quarters): row 32*warp + lane,
@@ -318,10 +366,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
     if (warp < 4) {
       const bool fin = mbar_wait(done_bar, 0);
       tc_fence_after();
-      // Sum of the eight accumulators: ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)) per token.
-      float acc[kTcAcc][kTcTok];
-#pragma unroll
-      for (int j = 0; j < kTcAcc; ++j) {
+      // Sum of the eight accumulators: ((a0+a1)+(a2+a3))+((a4+a5)+(a6+a7)) per
+      // token, built pair by pair so at most four accumulators are live.
+      auto load_acc = [&](int j, float (&a)[kTcTok]) {
         unsigned v[16];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -330,13 +377,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
             : "r"(tmem + (static_cast<uint32_t>(32 * warp) << 16) + j * kTcTok));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-        for (int t = 0; t < kTcTok; ++t) acc[j][t] = __uint_as_float(v[t]);
-      }
-      float total[kTcTok];
+        for (int t = 0; t < kTcTok; ++t) a[t] = __uint_as_float(v[t]);
+      };
+      // Sum of accumulators 4h .. 4h+3 as ((a0 + a1) + (a2 + a3)).
+      auto quad = [&](int h, float (&q)[kTcTok]) {
+        float x0[kTcTok], x1[kTcTok];
+        load_acc(4 * h, x0);
+        load_acc(4 * h + 1, x1);
 #pragma unroll
-      for (int t = 0; t < kTcTok; ++t)
-        total[t] = add_rn(add_rn(add_rn(acc[0][t], acc[1][t]), add_rn(acc[2][t], acc[3][t])),
-                          add_rn(add_rn(acc[4][t], acc[5][t]), add_rn(acc[6][t], acc[7][t])));
+        for (int t = 0; t < kTcTok; ++t) q[t] = add_rn(x0[t], x1[t]);
+        load_acc(4 * h + 2, x0);
+        load_acc(4 * h + 3, x1);
+#pragma unroll
+        for (int t = 0; t < kTcTok; ++t) q[t] = add_rn(q[t], add_rn(x0[t], x1[t]));
+      };
+      float total[kTcTok], upper[kTcTok];
+      quad(0, total);
+      quad(1, upper);
+#pragma unroll
+      for (int t = 0; t < kTcTok; ++t) total[t] = add_rn(total[t], upper[t]);
       const int row = row0 + 32 * warp + lane;
       if (!fin) record_status(p.status, kStatusMbarTimeout);
       if (fin && row < p.n) {
@@ -361,7 +420,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm_kernel(const __grid_con
   __syncthreads();
   if (warp == kTcMma) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols) : "memory");
   }
 }
 
@@ -413,7 +472,7 @@ int tc_gemm_launch(int kind, const void* x, int ldx, const void* w, const float*
   std::memset(&p, 0, sizeof(p));
   int rc = make_map(&p.tmap_w, kind == TC_I8_ROW ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                     wbytes, w, n, k, k, kind == TC_I8_ROW ? kTcBK : kTcAtom, kTcRows,
-                    kind == TC_I8_ROW ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B);
+                    CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   rc = make_map(&p.tmap_x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x, m, k, ldx, kTcAtom, kTcTok,
                 CU_TENSOR_MAP_SWIZZLE_128B);
