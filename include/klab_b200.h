@@ -86,6 +86,8 @@ extern "C" {
 #define KLAB_OPT_PROLOGUE 5    /* weight copies issued before the previous launch completes, per warp:
                                   (items into shared memory) + 16 * (items prefetched into L2);
                                   each part 0..3, -1 (default) the tuned choice */
+#define KLAB_OPT_MAX_TILE 6    /* largest token tile of the CUDA-core projection kernel: 1, 2, 4 (default) or 8;
+                                  results are the same bits for every tile */
 
 /* ---------------------------------------------------------------- projections */
 

@@ -35,6 +35,10 @@ std::atomic<int> g_opt_ctas_per_sm{0};  // 0: as many as fit
 // Prologue of the projection kernel: items copied into shared memory (low 4 bits)
 // and items prefetched into L2 (next 4 bits) before griddepcontrol.wait; -1: tuned.
 std::atomic<int> g_opt_prologue{-1};
+// Largest token tile of the CUDA-core kernel (1, 2, 4 or 8). Default 4: two
+// 4-token tiles with 16 warps beat one 8-token tile with 8 warps (config 3 M=8:
+// 63.3 -> 50.8 us; config 2 M=16 on CUDA cores: 111.7 -> 97.9 us).
+std::atomic<int> g_opt_max_tile{4};
 // Tensor-core path for token tiles: 0 off; 1 (default) INT8 per-row weights at
 // M >= 16, where the tile is a dense contraction; 2 INT8 per-row and BF16 weights
 // at M >= 2 (BF16 M-tiles then differ from M = 1 in the last bits; the
@@ -261,6 +265,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
     if (rc_tc != KLAB_E_ALIGN) return rc_tc;  // misaligned operands fall through to the CUDA cores
   }
   int mt = tile_for(m);
+  while (mt > g_opt_max_tile.load()) mt /= 2;
   int xmode = XM_SMEM;
   // 16-bit x is staged unconverted; the x budget is what the rings leave of the
   // CTA's shared memory, so wide token tiles keep x on chip instead of
@@ -676,6 +681,10 @@ int klab_set_option(int option, int value) {
       if (value != -1 && (value < 0 || (value & 15) > 3 || (value >> 4) > 3)) return KLAB_E_INVALID;
       g_opt_prologue.store(value);
       return 0;
+    case KLAB_OPT_MAX_TILE:
+      if (value != 1 && value != 2 && value != 4 && value != 8) return KLAB_E_INVALID;
+      g_opt_max_tile.store(value);
+      return 0;
     default: return KLAB_E_INVALID;
   }
 }
@@ -688,6 +697,7 @@ int klab_get_option(int option) {
     case KLAB_OPT_GENERIC: return g_opt_generic.load();
     case KLAB_OPT_CTAS_PER_SM: return g_opt_ctas_per_sm.load();
     case KLAB_OPT_PROLOGUE: return g_opt_prologue.load();
+    case KLAB_OPT_MAX_TILE: return g_opt_max_tile.load();
     default: return KLAB_E_INVALID;
   }
 }

@@ -52,7 +52,7 @@ def test_error_strings_and_options():
     assert _native.lib().lab_error_string(-1000).decode().startswith("Cannot load CUDA driver")
     for opt, values in ((_native.OPT_SPLIT, (-1, 0, 1)), (_native.OPT_PDL, (0, 1)), (_native.OPT_GENERIC, (1, 0)),
                         (_native.OPT_TENSOR, (0, 2, 1)), (_native.OPT_CTAS_PER_SM, (1, 0)),
-                        (_native.OPT_PROLOGUE, (0x00, 0x02, 0x10, 0x31, -1))):
+                        (_native.OPT_PROLOGUE, (0x00, 0x02, 0x10, 0x31, -1)), (_native.OPT_MAX_TILE, (8, 1, 2, 4))):
         before = _native.get_option(opt)
         for v in values:
             _native.set_option(opt, v)
@@ -62,6 +62,9 @@ def test_error_strings_and_options():
     for bad in (0x04, 0x40, 0x100, -2):  # each part of the prologue option is 0..3
         assert _native.lib().klab_set_option(_native.OPT_PROLOGUE, bad) == _native.E_INVALID
     assert _native.get_option(_native.OPT_PROLOGUE) == -1
+    for bad in (0, 3, 16):
+        assert _native.lib().klab_set_option(_native.OPT_MAX_TILE, bad) == _native.E_INVALID
+    assert _native.get_option(_native.OPT_MAX_TILE) == 4
 
 
 def test_invalid_arguments_rejected_before_any_device_work():

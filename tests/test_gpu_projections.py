@@ -131,7 +131,8 @@ def test_no_ftz_single_rne_known_answers():
 
 
 @pytest.mark.parametrize("k", [4096, 1024])
-def test_mtile_tokens_bit_identical_to_single_token(k):
+@pytest.mark.parametrize("max_tile", [4, 8])
+def test_mtile_tokens_bit_identical_to_single_token(native, k, max_tile):
     from klab_b200 import compressed_bf16 as cb
 
     n = 72
@@ -139,9 +140,13 @@ def test_mtile_tokens_bit_identical_to_single_token(k):
     x_all = dev_bf16(og.normal_bf16_bits(6, (17, k), 1.0))
     singles = torch.cat([cb.raw_linear(x_all[i:i + 1], w, threads=128, vector=8, output_dtype="bf16")
                          for i in range(17)])
-    for m in (2, 3, 4, 5, 7, 8, 9, 15, 16, 17):
-        y = cb.raw_linear(x_all[:m].contiguous(), w, threads=128, vector=8, output_dtype="bf16")
-        assert same_bits(y, singles[:m]), m
+    native.set_option(native.OPT_MAX_TILE, max_tile)
+    try:
+        for m in (2, 3, 4, 5, 7, 8, 9, 15, 16, 17):
+            y = cb.raw_linear(x_all[:m].contiguous(), w, threads=128, vector=8, output_dtype="bf16")
+            assert same_bits(y, singles[:m]), m
+    finally:
+        native.set_option(native.OPT_MAX_TILE, 4)
 
 
 def test_column_shards_bit_identical():
