@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 small-batch projection path (one JSON line on rank 0).
 
-Headline workload: the 32-layer Llama-3-8B-shaped
+Headline workload (benchmark config 5): the 32-layer Llama-3-8B-shaped
 projection chain at M=1 in one CUDA graph per token, column-sharded over the
 GPUs with an all-gather of `up` and `down` outputs per layer. value = tokens/s
 of the whole job (strong scaling: the per-token work is fixed as N grows).

@@ -1,4 +1,4 @@
-"""Projection chain of BASELINE config 5, column-sharded over ranks.
+"""Projection chain of benchmark config 5, column-sharded over ranks.
 
 Per layer (Llama-3-8B projection shapes, M tokens, BF16 weights and outputs):
   stage A: q 4096->4096, k 4096->1024, v 4096->1024, o 4096->4096,

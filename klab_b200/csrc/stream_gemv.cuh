@@ -5,9 +5,9 @@
 //   W_F16     FP16 weights (half_kernels.cu f16)
 //   W_F32     FP32 weights (kernels.cu gemv_*, projection_kernels.cu)
 //   W_CBF16   lossless BF16 codec v1 (compressed_kernels.cu:38-106, docs/bf16-format.md)
-//   W_I8_ROW  int8 + one fp32 scale per row
+//   W_I8_ROW  int8 + one fp32 scale per row (benchmark config 2)
 //   W_I8_G64  int8 + fp32 scale per 64 (int8_kernels.cu, int8_weights.py:23-35)
-//   W_FP4_G32H E2M1 + fp16 scale per 32
+//   W_FP4_G32H E2M1 + fp16 scale per 32 (benchmark config 3)
 //   W_FP4_G16E E2M1 + E4M3 scale per 16 + fp32 global (fp4_kernels.cu, fp4.py:33-60)
 //   W_LF32    lossless FP32 v1 (lossless_kernels.cu, lossless_weights.py)
 //   W_FP28    lossless FP32 as 28-bit codes (adaptive_kernels.cu fp28, packed_fp32.py)

@@ -1,6 +1,6 @@
 // Tensor-core (tcgen05) projection for token tiles: y[M, N] = x[M, K] . W[N, K]^T
 // with BF16 x, for weight formats whose values are exact in BF16: BF16 and INT8
-// with one FP32 scale per row. Used for M >= 2, where the
+// with one FP32 scale per row (benchmark config 2). Used for M >= 2, where the
 // CUDA-core kernel's per-token FMAs make it issue-bound.
 //
 // CTA = 128 weight rows (the MMA's M) x 16 tokens (its N, zero-padded) x all K.

@@ -3,7 +3,7 @@
 Two scale layouts share one kernel family:
 * the reference format (fp4.py:33-60): an E4M3 scale per 16 values and one
   FP32 global scale, x FP16/FP32 (reference) or BF16, FP32 output;
-* an FP16 scale per 32 values, x BF16, BF16 or FP32 output.
+* an FP16 scale per 32 values (benchmark config 3), x BF16, BF16 or FP32 output.
 Two codes per byte, low nibble = even k. E2M1 codes are converted with the
 hardware cvt.rn.f16x2.e2m1x2 and widened to FP32 in registers; each scale is
 applied once per group to the group's FP32 partial sum.
@@ -68,7 +68,7 @@ class FP4Weights:
 
 @dataclass(frozen=True)
 class FP4F16Weights:
-    """BASELINE format: packed [N,K/2] uint8, FP16 scales [N,K/32]."""
+    """Benchmark format: packed [N,K/2] uint8, FP16 scales [N,K/32]."""
 
     packed: torch.Tensor
     scales: torch.Tensor
@@ -126,7 +126,7 @@ def quantize_weights(w):
 
 
 def quantize_weights_f16(w):
-    """BASELINE format: per 32 values an FP16 scale = max|g|/6 (IEEE division, RNE to FP16),
+    """Benchmark format: per 32 values an FP16 scale = max|g|/6 (IEEE division, RNE to FP16),
     nearest-even E2M1 codes against that scale."""
     _check_source(w, 32)
     n, k = w.shape

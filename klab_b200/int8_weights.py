@@ -3,7 +3,7 @@
 Two scale layouts share one kernel family:
 * the reference format, an FP32 scale per 64 values (scales [N, K/64],
   int8_weights.py:23-35), x FP16/FP32 (the reference) or BF16, FP32 output;
-* per-row FP32 scales (scales [N]), x BF16, BF16 or FP32 output.
+* per-row FP32 scales (scales [N], benchmark config 2), x BF16, BF16 or FP32 output.
 Codes are decoded to exact FP32 in registers; the product with the scale is
 one FP32 multiply per 64-value group (per row for per-row scales).
 """
@@ -80,7 +80,7 @@ def quantize_weights(w):
 
 
 def quantize_weights_per_row(w):
-    """Per-row scale = max|row|/127 with an IEEE division,
+    """Per-row scale = max|row|/127 with an IEEE division (benchmark config 2),
     otherwise the reference's rounding rules."""
     _check_source(w, 1)
     n, k = w.shape

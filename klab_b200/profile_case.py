@@ -1,4 +1,4 @@
-"""A few launches of one BASELINE projection case through the public API, for a
+"""A few launches of one benchmark projection case through the public API, for a
 profiler to capture (e.g. `ncu -k regex:stream_gemv -s 2 -c 1 python -m
 klab_b200.profile_case --shape c2`). Seeded synthetic weights and activations
 with the configs' shapes and distributions; nothing is timed or checked here.

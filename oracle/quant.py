@@ -12,13 +12,13 @@ with round-to-nearest-even, exactly as the reference's torch code computes it:
 * INT8, reference format (int8_weights.py:15-35): per 64-value group,
   scale = max|w|/127 (clamped to FP32 tiny; 1.0 for an all-zero group),
   code = clamp(round_half_even(w / scale), -127, 127); dequant = code * scale.
-* INT8, per-row: one group per row, true IEEE division.
+* INT8, per-row (benchmark config 2): one group per row, true IEEE division.
 * FP4, reference format (fp4.py:21-60): global = max|W|/(448*6) (tiny-clamped,
   1.0 when W == 0); per 16 values an E4M3 scale = RNE_e4m3(min(max|g| / (6*global), 448));
   E2M1 codes by nearest value with ties to even (the bucketize + tie fix of
   fp4.py:53-58), sign bit from signbit(w / scale); low nibble = even k;
   dequant = e2m1 * (e4m3 * global).
-* FP4, FP16 scale per 32: scale = RNE_fp16(max|g| / 6)
+* FP4, FP16 scale per 32 (benchmark config 3): scale = RNE_fp16(max|g| / 6)
   with a true IEEE division;
   codes as above against that scale; dequant = e2m1 * scale (exact in FP32).
 """
@@ -75,7 +75,7 @@ def int8_quantize_g64(w: np.ndarray, semantics: str = "cuda"):
 
 
 def int8_quantize_row(w: np.ndarray):
-    """Per-row INT8: codes int8 [N,K], scales fp32 [N]."""
+    """Per-row INT8 (benchmark config 2): codes int8 [N,K], scales fp32 [N]."""
     n, k = _check_weights(w, 1)
     codes, scales = _int8_quantize_groups(w.reshape(n, 1, k), "cpu")
     return codes.reshape(n, k), scales.reshape(n)
@@ -177,7 +177,7 @@ def fp4_dequantize_e4m3(packed, scales, glob) -> np.ndarray:
 
 
 def fp4_quantize_f16(w: np.ndarray):
-    """FP4 with an FP16 scale per 32: packed [N,K/2],
+    """FP4 with an FP16 scale per 32 (benchmark config 3): packed [N,K/2],
     scales float16 [N,K/32]."""
     n, k = _check_weights(w, 32)
     blocks = w.reshape(n, k // 32, 32)

@@ -1,9 +1,9 @@
 """Generate golden fixtures for the oracle by running the reference's own code.
 
-Run in a checkout that has the reference tree (default /root/reference, or
-KLAB_REFERENCE=<path>); the GPU box and CI only read the committed .npz files:
+Run where the reference tree is available, with its path in KLAB_REFERENCE; the
+GPU box and CI only read the committed fixture files:
 
-    python tests/golden/make_golden.py
+    KLAB_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 What runs here is the reference's Python, unmodified:
   * compressed_bf16.pack_bits / unpack_bits, bf16_reference.decode_bf16
@@ -36,7 +36,7 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("KLAB_REFERENCE", "/root/reference"))
+REFERENCE = Path(os.environ["KLAB_REFERENCE"]) if os.environ.get("KLAB_REFERENCE") else None
 
 
 def _load(name: str):
@@ -269,8 +269,8 @@ def policy_fixtures(pp):
 
 
 def main():
-    if not REFERENCE.is_dir():
-        raise SystemExit(f"reference tree not found at {REFERENCE}")
+    if REFERENCE is None or not REFERENCE.is_dir():
+        raise SystemExit(f"set KLAB_REFERENCE to the reference tree (got {REFERENCE})")
     sys.path.insert(0, str(REFERENCE))
     sys.modules["kernel_lab"] = types.ModuleType("kernel_lab")
     cb = _load("compressed_bf16")
