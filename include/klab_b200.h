@@ -254,6 +254,12 @@ KLAB_API int klab_coded_linear(const void* x, const void* payload, const uint32_
 KLAB_API int klab_half_linear(const void* x, const void* w, int dtype, float* out, int m, int n, int k,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* out[M,K] = ((x + residual) * rsqrt(mean((x + residual)^2, row) + eps)) * weight[K],
+ * FP32, 1 <= K <= 8192, eps > 0. Replaces KernelLab.residual_rmsnorm and the op
+ * kernel_lab::residual_rmsnorm (kernel_lab.py:281-294, 343-353; kernels.cu:168-222). */
+KLAB_API int klab_residual_rmsnorm(const float* x, const float* residual, const float* weight, float* out, int m,
+                                   int k, float eps, void* stream);
+
 /* FP32 x, FP32 W, FP32 out.
  * Replaces KernelLab.matmul / warp_matmul / tiled_matmul / tiny_matmul
  * (kernel_lab.py:197-294, kernels.cu:13-166, adaptive_kernels.cu:3-41,

@@ -150,4 +150,49 @@ cudaError_t launch_fp4_dequant(const void* packed, const void* scales, int kind,
   return cudaGetLastError();
 }
 
+// y[r, :] = ((x + residual)[r, :] * rsqrt(mean((x + residual)[r, :]^2) + eps)) * weight
+// for FP32 rows of K <= 8192: one CTA of 256 threads per row, the summed row kept
+// in registers (thread t holds columns t, t + 256, ...). Reduction order: per
+// thread in column order, a butterfly within each warp, then the eight warp sums
+// in warp order; one rsqrtf. Same contract as kernels.cu:168-222.
+constexpr int kRmsThreads = 256;
+constexpr int kRmsMaxK = 8192;
+__global__ void __launch_bounds__(kRmsThreads) residual_rmsnorm_kernel(const float* __restrict__ x,
+                                                                       const float* __restrict__ residual,
+                                                                       const float* __restrict__ weight,
+                                                                       float* __restrict__ y, int k, float eps) {
+  constexpr int VALUES = kRmsMaxK / kRmsThreads;
+  constexpr int WARPS = kRmsThreads / 32;
+  __shared__ float partial[WARPS];
+  const long long base = static_cast<long long>(blockIdx.x) * k;
+  float v[VALUES];
+  float sum = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VALUES; ++i) {
+    const int col = threadIdx.x + i * kRmsThreads;
+    v[i] = col < k ? __fadd_rn(__ldg(x + base + col), __ldg(residual + base + col)) : 0.0f;
+    sum = __fmaf_rn(v[i], v[i], sum);
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  float total = partial[0];
+#pragma unroll
+  for (int w = 1; w < WARPS; ++w) total = __fadd_rn(total, partial[w]);
+  const float inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(total, static_cast<float>(k)), eps));
+#pragma unroll
+  for (int i = 0; i < VALUES; ++i) {
+    const int col = threadIdx.x + i * kRmsThreads;
+    if (col < k) y[base + col] = __fmul_rn(__fmul_rn(v[i], inv_rms), __ldg(weight + col));
+  }
+}
+
+cudaError_t launch_residual_rmsnorm(const float* x, const float* residual, const float* weight, float* y, int m,
+                                    int k, float eps, cudaStream_t stream) {
+  if (k > kRmsMaxK) return cudaErrorInvalidValue;
+  residual_rmsnorm_kernel<<<m, kRmsThreads, 0, stream>>>(x, residual, weight, y, k, eps);
+  return cudaGetLastError();
+}
+
 }  // namespace klab

@@ -639,6 +639,13 @@ int klab_int8_dequantize(const int8_t* codes, const float* scales, int group, fl
   return launch_int8_dequant(codes, scales, group, out, n, k, static_cast<cudaStream_t>(stream));
 }
 
+int klab_residual_rmsnorm(const float* x, const float* residual, const float* weight, float* out, int m, int k,
+                          float eps, void* stream) {
+  if (!x || !residual || !weight || !out || m <= 0 || k <= 0 || !(eps > 0.0f)) return KLAB_E_INVALID;
+  if (k > 8192 || static_cast<long long>(m) * k >= (1LL << 31) || m > 0x7fffffff) return KLAB_E_SHAPE;
+  return launch_residual_rmsnorm(x, residual, weight, out, m, k, eps, static_cast<cudaStream_t>(stream));
+}
+
 int klab_fp4_dequantize(const uint8_t* packed, const void* scales, int scale_kind, const float* gscale, float* out,
                         int n, int k, void* stream) {
   if (!packed || !scales || !out || n <= 0 || k <= 0) return KLAB_E_INVALID;

@@ -3,8 +3,10 @@
 KernelLab.matmul / warp_matmul / tiled_matmul / tiny_matmul keep their
 signatures, validation and FP32 contract; on B200 all of them run the sm_100a
 streaming kernel (FP32 weights and activations, FP32 accumulate and output),
-so their launch-configuration arguments are validated hints. The registered ops
-kernel_lab::matmul and kernel_lab::warp_matmul keep their schemas.
+so their launch-configuration arguments are validated hints. residual_rmsnorm
+(kernel_lab.py:281-294) runs klab_residual_rmsnorm. The registered ops
+kernel_lab::matmul, kernel_lab::warp_matmul and kernel_lab::residual_rmsnorm
+keep their schemas.
 """
 
 from __future__ import annotations
@@ -92,6 +94,25 @@ class KernelLab:
             raise ValueError("Vector loads require 16-byte alignment")
         return self._run(x, w, self.output(out, (m, n), x, w))
 
+    def residual_rmsnorm(self, x, residual, weight, eps=1e-6, threads=256, out=None):
+        """((x + residual) * rsqrt(mean((x + residual)^2) + eps)) * weight per row, FP32
+        (kernel_lab.py:281-294, kernels.cu:168-222); `threads` is a validated hint."""
+        self.validate(x, residual, weight)
+        if x.ndim != 2 or x.shape != residual.shape or weight.shape != (x.shape[1],):
+            raise ValueError("Expected x/residual=[M,K], weight=[K]")
+        m, k = x.shape
+        if not (m > 0 and 0 < k <= 8192 and m * k < 2 ** 31 and eps > 0):
+            raise ValueError("Require M>0, 1<=K<=8192, FP32 indexing, eps>0")
+        if threads not in (128, 256):
+            raise ValueError("threads must be 128 or 256")
+        out = self.output(out, x.shape, x, residual, weight)
+        stream = torch.cuda.current_stream(x.device)
+        rc = _native.lib().klab_residual_rmsnorm(x.data_ptr(), residual.data_ptr(), weight.data_ptr(),
+                                                 out.data_ptr(), m, k, float(eps), stream.cuda_stream)
+        _native.check(rc, "klab_residual_rmsnorm")
+        _native.record(stream, x, residual, weight, out)
+        return out
+
     def close(self):
         if not self._closed:
             torch.cuda.synchronize(self.device)
@@ -131,3 +152,16 @@ def warp_matmul(x: torch.Tensor, w: torch.Tensor, threads: int = 128, vector: in
 @warp_matmul.register_fake
 def _warp_matmul_fake(x, w, threads=128, vector=4):
     return x.new_empty((x.shape[0], w.shape[0]))
+
+
+@torch.library.custom_op("kernel_lab::residual_rmsnorm", mutates_args=(), device_types="cuda")
+def residual_rmsnorm(
+    x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6
+) -> torch.Tensor:
+    with torch.cuda.device(x.device):
+        return default_lab().residual_rmsnorm(x, residual, weight, eps=eps)
+
+
+@residual_rmsnorm.register_fake
+def _rmsnorm_fake(x, residual, weight, eps=1e-6):
+    return torch.empty_like(x)

@@ -46,3 +46,12 @@ def chain_reference_bf16(x_bits: np.ndarray, layers) -> np.ndarray:
     for w_bits in layers:
         h = round_bf16_bits(bf16_projection64(h, w_bits))
     return h
+
+
+def residual_rmsnorm64(x: np.ndarray, residual: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:
+    """FP64 restatement of the reference's fused residual RMSNorm
+    (kernels.cu:168-222, KernelLab.residual_rmsnorm kernel_lab.py:281-294):
+    v = x + residual, y = (v / sqrt(mean(v^2, row) + eps)) * weight."""
+    v = np.asarray(x, dtype=np.float64) + np.asarray(residual, dtype=np.float64)
+    inv = 1.0 / np.sqrt(np.mean(v * v, axis=1, keepdims=True) + float(eps))
+    return (v * inv) * np.asarray(weight, dtype=np.float64)[None, :]

@@ -76,6 +76,10 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert lib.lab_launch(None, 1, 1, 32, None, None) == _native.E_INVALID
     assert lib.lab_load_ptx(None, None) == _native.E_INVALID
     assert lib.klab_int8_linear(None, 0, None, None, 32, None, 0, 1, 1, 64, None, 0, None) == _native.E_UNSUPPORTED
+    assert lib.klab_residual_rmsnorm(None, None, None, None, 1, 64, 1e-6, None) == _native.E_INVALID
+    fake = 16  # never dereferenced: the shape checks reject these calls first
+    assert lib.klab_residual_rmsnorm(fake, fake, fake, fake, 1, 8193, 1e-6, None) == _native.E_SHAPE
+    assert lib.klab_residual_rmsnorm(fake, fake, fake, fake, 1, 64, 0.0, None) == _native.E_INVALID
 
 
 def test_workspace_sizes():
@@ -142,7 +146,7 @@ def test_fake_tensor_contracts():
     from torch._subclasses.fake_tensor import FakeTensorMode
 
     from klab_b200 import compressed_bf16 as cb
-    from klab_b200 import fp4, half_projection, int8_weights  # noqa: F401  (registers ops)
+    from klab_b200 import fp4, half_projection, int8_weights, kernel_lab  # noqa: F401  (registers ops)
 
     with FakeTensorMode():
         x = torch.empty(3, 128, dtype=torch.bfloat16)
@@ -158,4 +162,6 @@ def test_fake_tensor_contracts():
         y = torch.ops.kernel_lab.half_linear(torch.empty(2, 64, dtype=torch.bfloat16),
                                              torch.empty(5, 64, dtype=torch.bfloat16))
         assert tuple(y.shape) == (2, 5) and y.dtype == torch.float32
+        y = torch.ops.kernel_lab.residual_rmsnorm(torch.empty(3, 96), torch.empty(3, 96), torch.empty(96), 1e-5)
+        assert tuple(y.shape) == (3, 96) and y.dtype == torch.float32
     assert cb.kernel_names()[-1] == "cbf16_unpack" and len(cb.kernel_names()) == 33
