@@ -254,6 +254,30 @@ KLAB_API int klab_coded_linear(const void* x, const void* payload, const uint32_
 KLAB_API int klab_half_linear(const void* x, const void* w, int dtype, float* out, int m, int n, int k,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode elementwise ops, BF16 rows (two values per 32-bit word, d and inter even).
+ * x_out = RNE(res + y); xn_out = RNE(x * rsqrt(mean(x^2, row) + eps) * weight), in the
+ * reference kernel's order. Replaces add_rmsnorm_bf16 behind decode_attn.add_rmsnorm
+ * (research/l2-prefetch/src/decode_attn.cu:471-511, decode_attn.py:64-71). */
+KLAB_API int klab_add_rmsnorm(const void* res, const void* y, const void* weight, void* x_out, void* xn_out, int m,
+                              int d, float eps, void* stream);
+/* gu[M, 2*inter] = [gate | up] -> out[M, inter] = RNE(silu(gate) * up). Replaces silu_mul_bf16
+ * behind decode_attn.silu_mul (decode_attn.cu:513-527, decode_attn.py:74-81). */
+KLAB_API int klab_silu_mul(const void* gu, void* out, int m, int inter, void* stream);
+
+/* Fused: the projection out[M,N] = xn . W^T (BF16 W [N,K], BF16 out) with xn computed while
+ * x is staged, as klab_add_rmsnorm would (x_out, when not null, gets RNE(res + y)); bit-identical
+ * to klab_add_rmsnorm followed by klab_raw_linear. K % 8 == 0. No counterpart kernel in the
+ * reference: it fuses its add_rmsnorm_bf16 into the next projection (the "prologue fusion"
+ * named beside kernels.cu:168-222 and decode_attn.cu:473). */
+KLAB_API int klab_add_rmsnorm_linear(const void* res, const void* y, const void* norm_weight, float eps,
+                                     const void* w, void* out, void* x_out, int m, int n, int k, void* workspace,
+                                     size_t workspace_bytes, void* stream);
+/* Fused: out[M,N] = silu_mul(gu) . W^T with gu [M, 2*inter], W [N, inter]; bit-identical to
+ * klab_silu_mul followed by klab_raw_linear. inter % 8 == 0. No counterpart kernel in the
+ * reference (fuses its silu_mul_bf16, decode_attn.cu:513-527, into the down projection). */
+KLAB_API int klab_silu_mul_linear(const void* gu, const void* w, void* out, int m, int n, int inter,
+                                  void* workspace, size_t workspace_bytes, void* stream);
+
 /* out[M,K] = ((x + residual) * rsqrt(mean((x + residual)^2, row) + eps)) * weight[K],
  * FP32, 1 <= K <= 8192, eps > 0. Replaces KernelLab.residual_rmsnorm and the op
  * kernel_lab::residual_rmsnorm (kernel_lab.py:281-294, 343-353; kernels.cu:168-222). */

@@ -210,7 +210,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
                    const void* const* aux, const float* gscale, void* const* out, const int* ldo, const int* nrows,
                    int out_dt, int m, int k, void* ws, size_t ws_bytes, void* stream,
                    const klab_gather_t* gather = nullptr, const void* const* aux2 = nullptr,
-                   PlannedLaunch* plan_out = nullptr) {
+                   PlannedLaunch* plan_out = nullptr, const Prologue* pro = nullptr) {
   if (!x || !w || !out || !ldo || !nrows || nseg < 1 || nseg > kMaxSegs) return KLAB_E_INVALID;
   if (m <= 0 || k <= 0 || ldx < k) return KLAB_E_INVALID;
   if (wfmt < W_BF16 || wfmt > W_FP28) return KLAB_E_UNSUPPORTED;
@@ -254,9 +254,12 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
     }
   }
   const bool gathered_x = gather && gather->npeers > 0 && gather->wait_flags;
+  // A fused elementwise op computes x while staging it: BF16 x and weights, K % 8 == 0.
+  if (pro && (xdt != KLAB_DT_BF16 || (wfmt != W_BF16 && wfmt != W_CBF16) || k % 8 || gather))
+    return KLAB_E_UNSUPPORTED;
   // Token tiles of INT8 (and, optionally, BF16) weights go to the tensor cores.
   const int tensor = g_opt_tensor.load();
-  if (!plan_out && m >= 2 && nseg == 1 && !gather && xdt == KLAB_DT_BF16 &&
+  if (!plan_out && !pro && m >= 2 && nseg == 1 && !gather && xdt == KLAB_DT_BF16 &&
       ((wfmt == W_I8_ROW && (tensor == 2 || (tensor == 1 && m >= 16))) || (wfmt == W_BF16 && tensor == 2))) {
     const int rc_tc = tc_gemm_launch(wfmt == W_I8_ROW ? 1 : 0, x, ldx, w[0], wfmt == W_I8_ROW ?
                                      static_cast<const float*>(aux[0]) : nullptr, out[0], ldo[0],
@@ -284,7 +287,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
       break;
     }
     // Gathered x must be staged (its global reads bypass L1); never read it in place.
-    if (x_global_ok && !gathered_x) {
+    if (x_global_ok && !gathered_x && !pro) {
       xmode = XM_GLOBAL;
       break;
     }
@@ -311,6 +314,7 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   const int gmax = occ * info->sms / tiles > 0 ? occ * info->sms / tiles : 1;
 
   GemvParams p = {};
+  if (pro) p.pro = *pro;
   p.x = x;
   p.gscale = gscale;
   p.nseg = nseg;
@@ -418,6 +422,48 @@ int klab_raw_linear(const void* x, const void* w, void* out, int out_dtype, int 
                     size_t workspace_bytes, void* stream) {
   return run_gemv(W_BF16, KLAB_DT_BF16, x, k, w, nullptr, nullptr, out, n, out_dtype, m, n, k, workspace,
                   workspace_bytes, stream);
+}
+
+int klab_add_rmsnorm_linear(const void* res, const void* y, const void* norm_weight, float eps, const void* w,
+                            void* out, void* x_out, int m, int n, int k, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  if (!res || !y || !norm_weight || !w || !out || m <= 0 || n <= 0 || k <= 0 || !(eps > 0.0f)) return KLAB_E_INVALID;
+  if (k % 8) return KLAB_E_SHAPE;
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(res) | reinterpret_cast<uintptr_t>(y) |
+                        reinterpret_cast<uintptr_t>(norm_weight) | reinterpret_cast<uintptr_t>(x_out);
+  if (mis & 3) return KLAB_E_ALIGN;
+  Prologue pr = {};
+  pr.op = PRO_ADD_RMSNORM;
+  pr.ld = k;
+  pr.eps = eps;
+  pr.a = res;
+  pr.b = y;
+  pr.w = norm_weight;
+  pr.x_out = x_out;
+  pr.x_out_ld = k;
+  const void* ws_[1] = {w};
+  const void* as_[1] = {nullptr};
+  void* os_[1] = {out};
+  const int ldo_[1] = {n}, n_[1] = {n};
+  return run_gemv_multi(W_BF16, KLAB_DT_BF16, res, k, 1, ws_, as_, nullptr, os_, ldo_, n_, KLAB_DT_BF16, m, k,
+                        workspace, workspace_bytes, stream, nullptr, nullptr, nullptr, &pr);
+}
+
+int klab_silu_mul_linear(const void* gu, const void* w, void* out, int m, int n, int inter, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  if (!gu || !w || !out || m <= 0 || n <= 0 || inter <= 0) return KLAB_E_INVALID;
+  if (inter % 8) return KLAB_E_SHAPE;
+  if (reinterpret_cast<uintptr_t>(gu) & 3) return KLAB_E_ALIGN;
+  Prologue pr = {};
+  pr.op = PRO_SILU_MUL;
+  pr.ld = 2 * inter;
+  pr.a = gu;
+  const void* ws_[1] = {w};
+  const void* as_[1] = {nullptr};
+  void* os_[1] = {out};
+  const int ldo_[1] = {n}, n_[1] = {n};
+  return run_gemv_multi(W_BF16, KLAB_DT_BF16, gu, 2 * inter, 1, ws_, as_, nullptr, os_, ldo_, n_, KLAB_DT_BF16, m, inter,
+                        workspace, workspace_bytes, stream, nullptr, nullptr, nullptr, &pr);
 }
 
 int klab_coded_linear(const void* x, const void* payload, const uint32_t* metadata, void* out, int out_dtype, int m,
@@ -637,6 +683,19 @@ int klab_int8_dequantize(const int8_t* codes, const float* scales, int group, fl
   if (group != 0 && group != 64) return KLAB_E_UNSUPPORTED;
   if (group == 64 && k % 64) return KLAB_E_SHAPE;
   return launch_int8_dequant(codes, scales, group, out, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int klab_add_rmsnorm(const void* res, const void* y, const void* weight, void* x_out, void* xn_out, int m, int d,
+                     float eps, void* stream) {
+  if (!res || !y || !weight || !x_out || !xn_out || m <= 0 || d <= 0 || !(eps > 0.0f)) return KLAB_E_INVALID;
+  if (d % 2 || static_cast<long long>(m) * d >= (1LL << 31)) return KLAB_E_SHAPE;
+  return launch_add_rmsnorm(res, y, weight, x_out, xn_out, m, d, eps, static_cast<cudaStream_t>(stream));
+}
+
+int klab_silu_mul(const void* gu, void* out, int m, int inter, void* stream) {
+  if (!gu || !out || m <= 0 || inter <= 0) return KLAB_E_INVALID;
+  if (inter % 2 || static_cast<long long>(m) * inter * 2 >= (1LL << 31)) return KLAB_E_SHAPE;
+  return launch_silu_mul(gu, out, m, inter, static_cast<cudaStream_t>(stream));
 }
 
 int klab_residual_rmsnorm(const float* x, const float* residual, const float* weight, float* out, int m, int k,

@@ -16,6 +16,9 @@ cudaError_t launch_int8_dequant(const void* codes, const float* scales, int grou
                                 cudaStream_t stream);
 cudaError_t launch_fp4_dequant(const void* packed, const void* scales, int kind, const float* gscale, float* out,
                                int n, int k, cudaStream_t stream);
+cudaError_t launch_add_rmsnorm(const void* res, const void* y, const void* w, void* x, void* xn, int m, int d,
+                               float eps, cudaStream_t stream);
+cudaError_t launch_silu_mul(const void* gu, void* out, int m, int inter, cudaStream_t stream);
 cudaError_t launch_residual_rmsnorm(const float* x, const float* residual, const float* weight, float* y, int m,
                                     int k, float eps, cudaStream_t stream);
 cudaError_t launch_lossless_unpack(const void* mantissa, const void* exponents, const void* payload,

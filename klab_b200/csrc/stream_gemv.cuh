@@ -43,6 +43,7 @@
 // the same bits as one warp doing the whole row.
 #pragma once
 #include "common.cuh"
+#include "decode_ops.cuh"
 #include "lossless_f32.cuh"
 
 namespace klab {
@@ -195,8 +196,25 @@ struct Gather {
   unsigned* done;                 // CTA completion counter, zero between launches
 };
 
+// Elementwise op fused into the x staging (BF16 x, BF16 weights): x is not read
+// from `x` but computed per token from the op's inputs, with the arithmetic of
+// the standalone kernels (decode_ops.cuh), so the projection equals the
+// standalone op followed by the plain projection, bit for bit.
+enum ProOp : int { PRO_NONE = 0, PRO_ADD_RMSNORM = 1, PRO_SILU_MUL = 2 };
+struct Prologue {
+  int op;
+  int ld;              // row stride of a / b in elements (BF16)
+  float eps;
+  const void* a;       // ADD_RMSNORM: residual [M, K]; SILU_MUL: [gate | up] [M, 2K]
+  const void* b;       // ADD_RMSNORM: y [M, K]
+  const void* w;       // ADD_RMSNORM: norm weight [K]
+  void* x_out;         // ADD_RMSNORM: RNE(residual + y) [M, K] (written by the grid's column 0)
+  int x_out_ld;
+};
+
 struct GemvParams {
   Gather gather;
+  Prologue pro;
   const void* x;        // [M, ldx] activations (X format)
   const float* gscale;  // W_FP4_G16E global scale (device scalar)
   Segment seg[kMaxSegs];
@@ -317,9 +335,69 @@ __device__ __forceinline__ uint4 bf16x8_to_f16x8_scaled(const uint4 v, float sca
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// x staging with a fused elementwise op (16-bit staging, K % 8 == 0): each
+// 16-byte unit (8 values = 4 pairs) of token t is computed from the op's inputs.
+template <int F, int MT>
+__device__ void stage_x_prologue(const GemvParams& p, int tile, unsigned char* xs, int segs) {
+  constexpr int VALS = WTraits<F>::VALS;
+  constexpr int NV = XLayout<F, XM_SMEM16>::NV;
+  __shared__ float red[8];
+  __shared__ float s_inv[MT];
+  const Prologue& pr = p.pro;
+  const int kpad = segs * 32 * VALS;
+  const int upt = kpad / 8;
+  if (pr.op == PRO_ADD_RMSNORM) {
+    for (int t = 0; t < MT; ++t) {
+      const int token = tile * MT + t;
+      if (token >= p.m) break;  // uniform
+      const unsigned* res2 = static_cast<const unsigned*>(pr.a) + static_cast<long long>(token) * (pr.ld / 2);
+      const unsigned* y2 = static_cast<const unsigned*>(pr.b) + static_cast<long long>(token) * (pr.ld / 2);
+      unsigned* x2 = blockIdx.x == 0 && pr.x_out
+                         ? static_cast<unsigned*>(pr.x_out) + static_cast<long long>(token) * (pr.x_out_ld / 2)
+                         : nullptr;
+      const float inv = add_rmsnorm_inv(res2, y2, x2, p.k, pr.eps, red);
+      if (threadIdx.x == 0) s_inv[t] = inv;
+      __syncthreads();  // red is free again; s_inv[t] is visible
+    }
+  }
+  for (int u = threadIdx.x; u < MT * upt; u += blockDim.x) {
+    const int t = u / upt;
+    const int col0 = (u - t * upt) * 8;
+    const int token = tile * MT + t;
+    unsigned v[4] = {0u, 0u, 0u, 0u};
+    if (token < p.m && col0 < p.k) {
+      const long long row = static_cast<long long>(token) * (pr.ld / 2);
+      const int i0 = col0 / 2;
+      if (pr.op == PRO_ADD_RMSNORM) {
+        const unsigned* res2 = static_cast<const unsigned*>(pr.a) + row;
+        const unsigned* y2 = static_cast<const unsigned*>(pr.b) + row;
+        const unsigned* w2 = static_cast<const unsigned*>(pr.w);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          v[e] = add_rmsnorm_pair(__ldg(res2 + i0 + e), __ldg(y2 + i0 + e), __ldg(w2 + i0 + e), s_inv[t]);
+      } else {
+        const unsigned* g2 = static_cast<const unsigned*>(pr.a) + row;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[e] = silu_mul_pair(__ldg(g2 + i0 + e), __ldg(g2 + p.k / 2 + i0 + e));
+      }
+    }
+    const int g = col0 / (32 * VALS);
+    const int r = col0 - g * 32 * VALS;
+    const int l = r / VALS;
+    const int i = (r - l * VALS) / 8;
+    *reinterpret_cast<uint4*>(xs + ((((t * segs + g) * NV + i) * 32 + l) << 4)) = make_uint4(v[0], v[1], v[2], v[3]);
+  }
+}
+
 template <int F, int X, int XM, int MT>
 __device__ void stage_x(const GemvParams& p, int tile, unsigned char* xs, int segs, XHalfState* xh) {
   constexpr bool HALF = HalfX<F, X, XM>::value;
+  if constexpr (XM == XM_SMEM16 && X == X_BF16 && !HALF) {
+    if (p.pro.op != PRO_NONE) {
+      stage_x_prologue<F, MT>(p, tile, xs, segs);
+      return;
+    }
+  }
   constexpr int VALS = WTraits<F>::VALS;
   constexpr int EB = XLayout<F, XM>::EB;
   constexpr int PER = 16 / EB;  // values per 16-byte unit

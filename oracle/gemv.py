@@ -55,3 +55,24 @@ def residual_rmsnorm64(x: np.ndarray, residual: np.ndarray, weight: np.ndarray, 
     v = np.asarray(x, dtype=np.float64) + np.asarray(residual, dtype=np.float64)
     inv = 1.0 / np.sqrt(np.mean(v * v, axis=1, keepdims=True) + float(eps))
     return (v * inv) * np.asarray(weight, dtype=np.float64)[None, :]
+
+
+def add_rmsnorm_ref(res_bits: np.ndarray, y_bits: np.ndarray, w_bits: np.ndarray, eps: float):
+    """The reference's add_rmsnorm (research/l2-prefetch/src/decode_attn.cu:471-511):
+    x = RNE_bf16(fp32(res) + fp32(y)) exactly (bits), and xn in FP64 from that x:
+    x / sqrt(mean(x^2) + eps) * w (the kernel rounds xn once to BF16)."""
+    from .bf16 import bf16_values, round_bf16_bits
+
+    s32 = (bf16_values(res_bits).astype(np.float32) + bf16_values(y_bits).astype(np.float32))
+    x_bits = round_bf16_bits(s32.astype(np.float64))
+    x = bf16_values(x_bits)
+    inv = 1.0 / np.sqrt(np.mean(x * x, axis=1, keepdims=True) + float(eps))
+    return x_bits, (x * inv) * bf16_values(w_bits)[None, :]
+
+
+def silu_mul64(gu_bits: np.ndarray) -> np.ndarray:
+    """silu(gate) * up in FP64 for gu = [gate | up] (decode_attn.cu:513-527)."""
+    from .bf16 import bf16_values
+
+    g, u = np.split(bf16_values(gu_bits), 2, axis=1)
+    return g / (1.0 + np.exp(-g)) * u

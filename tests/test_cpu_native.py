@@ -77,9 +77,19 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert lib.lab_load_ptx(None, None) == _native.E_INVALID
     assert lib.klab_int8_linear(None, 0, None, None, 32, None, 0, 1, 1, 64, None, 0, None) == _native.E_UNSUPPORTED
     assert lib.klab_residual_rmsnorm(None, None, None, None, 1, 64, 1e-6, None) == _native.E_INVALID
+    assert lib.klab_add_rmsnorm(None, None, None, None, None, 1, 64, 1e-6, None) == _native.E_INVALID
+    assert lib.klab_silu_mul(None, None, 1, 64, None) == _native.E_INVALID
+    assert lib.klab_add_rmsnorm_linear(None, None, None, 1e-6, None, None, None, 1, 8, 64, None, 0, None) \
+        == _native.E_INVALID
+    assert lib.klab_silu_mul_linear(None, None, None, 1, 8, 64, None, 0, None) == _native.E_INVALID
     fake = 16  # never dereferenced: the shape checks reject these calls first
     assert lib.klab_residual_rmsnorm(fake, fake, fake, fake, 1, 8193, 1e-6, None) == _native.E_SHAPE
     assert lib.klab_residual_rmsnorm(fake, fake, fake, fake, 1, 64, 0.0, None) == _native.E_INVALID
+    assert lib.klab_add_rmsnorm(fake, fake, fake, fake, fake, 1, 63, 1e-6, None) == _native.E_SHAPE
+    assert lib.klab_silu_mul(fake, fake, 1, 63, None) == _native.E_SHAPE
+    assert lib.klab_add_rmsnorm_linear(fake, fake, fake, 1e-6, fake, fake, None, 1, 8, 60, None, 0, None) \
+        == _native.E_SHAPE
+    assert lib.klab_silu_mul_linear(fake, fake, fake, 1, 8, 60, None, 0, None) == _native.E_SHAPE
 
 
 def test_workspace_sizes():
