@@ -282,6 +282,51 @@ def bench_projections(torch, peak, quick=False):
     return results
 
 
+def bench_decode_attention(torch, peak, quick=False):
+    """Decode attention with the KV append (klab_b200.decode_attn, Llama-3-8B heads: 32 query, 8 kv,
+    head 64, capacity 4096) over a ring of caches larger than L2, with torch's SDPA on the same
+    caches. bytes = the K and V rows read (L + 1 per kv head) + q, the new rows and the output."""
+    import torch.nn.functional as F
+
+    from klab_b200.decode_attn import decode_attention
+
+    dev = torch.device("cuda")
+    stream = torch.cuda.Stream()
+    heads, kv, cap = 32, 8, 4096
+    per = 2 * kv * cap * 64 * 2
+    ring = max(8, math.ceil(4 * L2_BYTES / per))
+    gen = torch.Generator(device=dev).manual_seed(21)
+    caches = [(torch.randn((kv, cap, 64), generator=gen, device=dev).to(torch.bfloat16),
+               torch.randn((kv, cap, 64), generator=gen, device=dev).to(torch.bfloat16)) for _ in range(ring)]
+    q = torch.randn(heads * 64, generator=gen, device=dev).to(torch.bfloat16)
+    kn = torch.randn(kv * 64, generator=gen, device=dev).to(torch.bfloat16)
+    vn = torch.randn(kv * 64, generator=gen, device=dev).to(torch.bfloat16)
+    out = torch.empty(heads * 64, device=dev, dtype=torch.bfloat16)
+    rows = []
+    for length in ((4095,) if quick else (255, 1023, 4095)):
+        def ours(i):
+            decode_attention(q, kn, vn, caches[i][0], caches[i][1], length, out=out)
+
+        def sdpa(i):
+            F.scaled_dot_product_attention(q.view(1, heads, 1, 64), caches[i][0][:, :length + 1].unsqueeze(0),
+                                           caches[i][1][:, :length + 1].unsqueeze(0), enable_gqa=True)
+
+        nbytes = 2 * kv * (length + 1) * 64 * 2 + heads * 64 * 2 * 2 + 2 * kv * 64 * 2
+        g = graph_of(torch, lambda: [ours(i) for i in range(ring)], stream)
+        us = time_graph(torch, g, ring, 5 if quick else 15)
+        del g
+        gv = graph_of(torch, lambda: [sdpa(i) for i in range(ring)], stream)
+        vus = time_graph(torch, gv, ring, 5 if quick else 15)
+        del gv
+        rows.append({"heads": heads, "kv_heads": kv, "length": length, "capacity": cap, "bytes": nbytes,
+                     "us": round(us, 3), "gbs": round(nbytes / us / 1e3, 1),
+                     "frac_of_measured_peak": round(nbytes / us / 1e3 / peak, 4), "sdpa_us": round(vus, 3),
+                     "speedup_vs_sdpa": round(vus / us, 3)})
+    del caches
+    torch.cuda.empty_cache()
+    return rows
+
+
 # ---------------------------------------------------------------- dominant kernel roofline
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one gate launch (14336 x 4096 BF16,
@@ -483,12 +528,13 @@ def main(argv=None):
     roofline["peak_kind"] = peak_kind
     status = _native.device_status(clear=True)
 
-    projections = None
+    projections = attention = None
     if world == 1 and not args.no_projections:
         del chain
         torch.cuda.empty_cache()
         chain = None
         projections = bench_projections(torch, peak, quick=args.quick)
+        attention = bench_decode_attention(torch, peak, quick=args.quick)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -522,6 +568,8 @@ def main(argv=None):
             line["cpu_baseline"] = cpu
         if projections is not None:
             line["projections"] = projections
+        if attention is not None:
+            line["decode_attention"] = attention
         print(json.dumps(line), flush=True)
 
     if chain is not None:

@@ -264,6 +264,21 @@ KLAB_API int klab_add_rmsnorm(const void* res, const void* y, const void* weight
  * behind decode_attn.silu_mul (decode_attn.cu:513-527, decode_attn.py:74-81). */
 KLAB_API int klab_silu_mul(const void* gu, void* out, int m, int inter, void* stream);
 
+/* M=1 decode attention with the new K/V row appended: writes k_new/v_new at row `len` of each kv
+ * head's cache and out = softmax(q K^T * scale) V over len + 1 tokens; q [heads*64], k_new/v_new
+ * [kv_heads*64], caches [kv_heads, max_len, 64], BF16, 16-byte aligned (out and scratch too);
+ * heads / kv_heads <= 16; max_len <= 65536. len_ptr (device int32), when not null, replaces len and
+ * the launch shape depends on max_len only (graph replay with a growing length; a device length
+ * outside [0, max_len) sets device status 3 and touches nothing). scratch: heads * ceil(max_len /
+ * 64) * 66 floats always suffice (scratch_floats is checked); tickets: kv_heads zeroed words, left
+ * zero; one stream at a time per scratch/tickets pair. Replaces decode_attn_v4/v4d/v5_bf16 behind
+ * decode_attn.decode_attention(_dynamic) (research/l2-prefetch/src/decode_attn.cu:258-460,
+ * decode_attn.py:20-107). */
+KLAB_API int klab_decode_attention(const void* q, const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                                   void* out, float* scratch, long long scratch_floats, unsigned* tickets,
+                                   const int* len_ptr, int len, int max_len, int heads, int kv_heads, float scale,
+                                   void* stream);
+
 /* Fused: the projection out[M,N] = xn . W^T (BF16 W [N,K], BF16 out) with xn computed while
  * x is staged, as klab_add_rmsnorm would (x_out, when not null, gets RNE(res + y)); bit-identical
  * to klab_add_rmsnorm followed by klab_raw_linear. K % 8 == 0. No counterpart kernel in the
@@ -368,7 +383,9 @@ KLAB_API int klab_l2_prefetch(const void* p, long long bytes, int blocks, int th
 
 KLAB_API int klab_set_option(int option, int value);
 KLAB_API int klab_get_option(int option);
-/* Read the current device's status word (0 = no device-side error); clear it when clear != 0. */
+/* Read the current device's status word (0 = no device-side error; 1 = a bulk copy wait gave up,
+ * 2 = a peer flag wait gave up, 3 = a length read from device memory was out of range); clear it
+ * when clear != 0. */
 KLAB_API int klab_device_status(int clear);
 KLAB_API const char* klab_error_string(int code);
 KLAB_API int klab_version(void);

@@ -54,6 +54,8 @@ _SIGNATURES = {
     "klab_residual_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, ct.c_float, _P]),
     "klab_add_rmsnorm": (_I, [_P, _P, _P, _P, _P, _I, _I, ct.c_float, _P]),
     "klab_silu_mul": (_I, [_P, _P, _I, _I, _P]),
+    "klab_decode_attention": (_I, [_P, _P, _P, _P, _P, _P, _P, ct.c_longlong, _P, _P, _I, _I, _I, _I, ct.c_float,
+                                    _P]),
     "klab_add_rmsnorm_linear": (_I, [_P, _P, _P, ct.c_float, _P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "klab_silu_mul_linear": (_I, [_P, _P, _P, _I, _I, _I, _P, _SZ, _P]),
     "klab_int8_linear": (_I, [_P, _I, _P, _P, _I, _P, _I, _I, _I, _I, _P, _SZ, _P]),

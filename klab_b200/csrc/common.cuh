@@ -19,6 +19,7 @@ enum DeviceStatus : int {
   kStatusOk = 0,
   kStatusMbarTimeout = 1,     // a bulk copy did not complete within the limit
   kStatusFlagTimeout = 2,     // a peer flag was not raised within the limit
+  kStatusBadLength = 3,       // a length read from device memory was out of range
 };
 
 // Iteration limit for every spin on an mbarrier or a flag. try_wait suspends for a

@@ -5,7 +5,9 @@ with the configs' shapes and distributions; nothing is timed or checked here.
 
 Shapes: c1 (BF16 4096x4096, M=1), gate (BF16 14336x4096, M=1), c2 / c2m4 / c2m16
 (INT8 per row 14336x4096, M=1/4/16), c3 / c3m8 (E2M1 + FP16 scale per 32,
-8192x8192, M=1/8), c4 (lossless-coded BF16 4096x4096, M=1).
+8192x8192, M=1/8), c4 (lossless-coded BF16 4096x4096, M=1); attn (decode
+attention with the KV append, 32 query / 8 kv heads of 64, 4095 cached tokens of
+a 4096-token cache).
 """
 
 from __future__ import annotations
@@ -17,7 +19,7 @@ import torch
 from . import compressed_bf16 as cb
 from . import fp4, int8_weights
 
-SHAPES = ("c1", "gate", "c2", "c2m4", "c2m16", "c3", "c3m8", "c4")
+SHAPES = ("c1", "gate", "c2", "c2m4", "c2m16", "c3", "c3m8", "c4", "attn")
 
 
 def case(shape, device="cuda"):
@@ -47,6 +49,12 @@ def case(shape, device="cuda"):
         q = int8_weights.quantize_weights_per_row(normal((14336, 4096), 0.02))
         x = normal(({"c2": 1, "c2m4": 4, "c2m16": 16}[shape], 4096)).to(torch.bfloat16)
         return lambda: int8_weights.fused_linear(x, q.codes, q.scales, output_dtype=torch.bfloat16)
+    if shape == "attn":
+        from .decode_attn import decode_attention
+
+        kc, vc = normal((8, 4096, 64)).to(torch.bfloat16), normal((8, 4096, 64)).to(torch.bfloat16)
+        q, kn, vn = (normal((n,)).to(torch.bfloat16) for n in (32 * 64, 8 * 64, 8 * 64))
+        return lambda: decode_attention(q, kn, vn, kc, vc, 4095)
     raise ValueError(f"unknown shape {shape!r}; expected one of {SHAPES}")
 
 

@@ -82,6 +82,8 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert lib.klab_add_rmsnorm_linear(None, None, None, 1e-6, None, None, None, 1, 8, 64, None, 0, None) \
         == _native.E_INVALID
     assert lib.klab_silu_mul_linear(None, None, None, 1, 8, 64, None, 0, None) == _native.E_INVALID
+    assert lib.klab_decode_attention(None, None, None, None, None, None, None, 0, None, None, 0, 64, 8, 2, 0.125,
+                                     None) == _native.E_INVALID
     fake = 16  # never dereferenced: the shape checks reject these calls first
     assert lib.klab_residual_rmsnorm(fake, fake, fake, fake, 1, 8193, 1e-6, None) == _native.E_SHAPE
     assert lib.klab_residual_rmsnorm(fake, fake, fake, fake, 1, 64, 0.0, None) == _native.E_INVALID
@@ -90,6 +92,12 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert lib.klab_add_rmsnorm_linear(fake, fake, fake, 1e-6, fake, fake, None, 1, 8, 60, None, 0, None) \
         == _native.E_SHAPE
     assert lib.klab_silu_mul_linear(fake, fake, fake, 1, 8, 60, None, 0, None) == _native.E_SHAPE
+    assert lib.klab_decode_attention(fake, fake, fake, fake, fake, fake, fake, 1 << 20, fake, None, 0, 64, 34, 2,
+                                     0.125, None) == _native.E_SHAPE  # 17 query heads per kv head
+    assert lib.klab_decode_attention(fake, fake, fake, fake, fake, fake, fake, 1 << 20, fake, None, 64, 64, 8, 2,
+                                     0.125, None) == _native.E_SHAPE  # len + 1 > capacity
+    assert lib.klab_decode_attention(fake, fake, fake, fake, fake, fake, fake, 1 << 20, fake, fake, 0, 65537, 8, 2,
+                                     0.125, None) == _native.E_SHAPE  # capacity above 65536
 
 
 def test_workspace_sizes():
