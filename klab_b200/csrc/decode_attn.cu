@@ -41,7 +41,10 @@ namespace {
 
 constexpr int kHD = 64;             // head dimension
 constexpr int kRowBytes = kHD * 2;  // one BF16 K or V row
-constexpr int kMinTile = 64;
+#ifndef KLAB_ATTN_MIN_TILE
+#define KLAB_ATTN_MIN_TILE 64  // smallest tile the planner cuts the span into (a multiple of 64)
+#endif
+constexpr int kMinTile = KLAB_ATTN_MIN_TILE;
 constexpr int kMaxTile = 512;
 constexpr int kMaxGroup = 16;       // query heads per kv head
 constexpr int kAttnThreads = 256;
