@@ -9,22 +9,28 @@
 // length is read from device memory) is cut into `splits` tiles of `tile` tokens
 // (a multiple of 64, at most 512). CTA (kv head, split) serves every query head
 // of its group, so each K/V row crosses HBM once:
-//   1. K rows are loaded with coalesced 16-byte loads and stored XOR-swizzled
-//      (chunk i of row r at chunk i ^ (r mod 8)); V rows arrive by one 1-D bulk
-//      copy, overlapped with the scores. The CTA whose tile holds position `len`
-//      writes the new K/V row into the cache and into its tile.
-//   2. Scores: thread per token, four heads at a time. The swizzle keeps the K
-//      reads conflict-free while every thread reads the same q chunk (broadcast).
-//   3. Softmax partial (m, l): warp per head. p is stored [token][head].
-//   4. o = sum_j p_j V_j: thread per (8-dimension chunk, token class), four heads
-//      at a time (one 16-byte V read and one 16-byte p read per 32 FMAs); token
-//      classes are summed in a fixed order (shuffles, then warps in order).
+//   1. K and V rows are loaded with coalesced 16-byte loads (sixteen in flight per
+//      thread) and stored XOR-swizzled (chunk i of row r at chunk i ^ (r mod 8)),
+//      which keeps the fragment loads below conflict-free. The CTA whose tile
+//      holds position `len` writes the new K/V row into the cache and its tiles.
+//   2. Scores on the tensor cores (mma.sync m16n8k16, BF16 in, FP32 out): the
+//      group's query heads (at most 16) are the 16 rows of the A fragment, loaded
+//      once from global memory; warp w takes a contiguous run of tokens and reads
+//      K fragments with ldmatrix. Tokens past the end are masked to -inf.
+//   3. Softmax partials in registers: per-warp row maxima through shared memory,
+//      p = exp(s - m), per-warp row sums.
+//   4. O = P V on the tensor cores: p is split into hi + lo BF16 halves (so the
+//      product keeps close to FP32 accuracy) that feed the A fragments straight
+//      from the score accumulators; V fragments come from transposing ldmatrix.
+//      The warps' 16 x 64 partials are summed in warp order through shared memory.
 //   5. Merge of the splits with weights exp(m_c - max m):
 //      - cluster mode (splits <= the cluster limit): the splits of one kv head
 //        form a thread-block cluster; each CTA keeps (m, l, o[64]) per head in
 //        shared memory and the cluster reads them over distributed shared memory;
 //      - ticket mode (longer spans): records go to global scratch and the last
 //        CTA of a kv head (atomic ticket) merges them and resets the ticket.
+// The two contractions are 16-row matrix products: warp-level mma.sync fits them,
+// where a tcgen05 tile (64 or 128 rows) would leave most of its rows empty.
 // FP32 arithmetic, the fast exp intrinsic, one RNE to BF16. A device length
 // outside [0, capacity) leaves the caches and the output untouched and sets the
 // device status word (kStatusBadLength).
@@ -45,6 +51,12 @@ constexpr int kRowBytes = kHD * 2;  // one BF16 K or V row
 #define KLAB_ATTN_MIN_TILE 64  // smallest tile the planner cuts the span into (a multiple of 64)
 #endif
 constexpr int kMinTile = KLAB_ATTN_MIN_TILE;
+#ifndef KLAB_ATTN_CLUSTER
+#define KLAB_ATTN_CLUSTER 1  // 1: merge over a thread-block cluster when one covers the span
+#endif
+#ifndef KLAB_ATTN_SMEM_FLOOR
+#define KLAB_ATTN_SMEM_FLOOR 0  // minimum dynamic shared memory per CTA (bytes): limits CTAs per SM
+#endif
 constexpr int kMaxTile = 512;
 constexpr int kMaxGroup = 16;       // query heads per kv head
 constexpr int kAttnThreads = 256;
@@ -53,6 +65,7 @@ constexpr int kRecord = kHD + 2;    // (m, l, o[64]) per (head, split)
 constexpr int kMaxSpan = 65536;
 constexpr int kMaxClusterSplits = 16;  // the largest (non-portable) cluster
 constexpr size_t kMaxSmem = 227 * 1024;
+constexpr float kNegInf = -__builtin_huge_valf();
 
 struct AttnParams {
   const unsigned short* q;
@@ -66,28 +79,31 @@ struct AttnParams {
   const int* len_ptr;
   int* status;
   int len_value, max_len, heads, kv_heads, splits, tile;
+  int tpw;  // tokens per warp: a multiple of 16; 8 * tpw >= tile
   float scale;
 };
 
 struct SmemLayout {
-  size_t ks, vs, qs, sc, red, part, wts, ml, bar, total;
+  size_t ks, vs, red, part, wts, ml, stats, tk, total;
 };
 
-__host__ __device__ inline int group4(int group) { return (group + 3) & ~3; }
+constexpr int kRedStride = kHD + 8;  // floats per (warp, head row) of the output partials
+
+// Tokens per warp for a tile: 16-token steps of the tensor-core fragments.
+__host__ __device__ inline int tokens_per_warp(int tile) { return ((tile + kWarps - 1) / kWarps + 15) & ~15; }
 
 __host__ __device__ inline SmemLayout layout_for(int tile, int group, int splits, bool ticket) {
-  const size_t g4 = group4(group);
+  const size_t rows = static_cast<size_t>(kWarps) * tokens_per_warp(tile);  // tile rounded up
   SmemLayout s;
   s.ks = 0;
-  s.vs = s.ks + static_cast<size_t>(tile) * kRowBytes;
-  s.qs = s.vs + static_cast<size_t>(tile) * kRowBytes;
-  s.sc = s.qs + g4 * kHD * 4;
-  s.red = s.sc + static_cast<size_t>(tile) * g4 * 4;
-  s.part = s.red + static_cast<size_t>(kWarps) * 4 * kHD * 4;  // per warp: 4 heads x 64 dims
+  s.vs = s.ks + rows * kRowBytes;
+  s.red = s.vs + rows * kRowBytes;
+  s.part = s.red + static_cast<size_t>(kWarps) * 16 * kRedStride * 4;  // per warp: 16 head rows
   s.wts = s.part + static_cast<size_t>(group) * kRecord * 4;
   s.ml = s.wts + (ticket ? 2 * static_cast<size_t>(group) * splits * 4 : 0);
-  s.bar = (s.ml + 2 * kMaxGroup * 4 + 15) / 16 * 16;
-  s.total = s.bar + 16;
+  s.stats = s.ml + 2 * kMaxGroup * 4;
+  s.tk = (s.stats + 2 * kWarps * 16 * 4 + 15) / 16 * 16;
+  s.total = s.tk + 16;
   return s;
 }
 
@@ -115,6 +131,43 @@ __device__ __forceinline__ float warp_max(float m) {
 
 __device__ __forceinline__ unsigned short rne_bf16(float v) { return f32_to_bf16_rn(v); }
 
+// D += A (16x16, BF16, row) * B (16x8, BF16, col) with FP32 accumulation.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldsm_x4(unsigned addr, unsigned (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_trans(unsigned addr, unsigned (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// Two floats as BF16 (RNE), x0 in the low half.
+__device__ __forceinline__ unsigned pack_bf16x2(float x0, float x1) {
+  return static_cast<unsigned>(f32_to_bf16_rn(x0)) | (static_cast<unsigned>(f32_to_bf16_rn(x1)) << 16);
+}
+
+// p = hi + lo with hi, lo BF16: the pair's hi word and the residuals' lo word.
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, unsigned& hi, unsigned& lo) {
+  hi = pack_bf16x2(x0, x1);
+  lo = pack_bf16x2(__fsub_rn(x0, bf16lo(hi)), __fsub_rn(x1, bf16hi(hi)));
+}
+
+// Byte offset of 16-byte chunk `ch` of row `r` in a swizzled 128-byte-row tile.
+__device__ __forceinline__ unsigned swz(int r, int ch) {
+  return static_cast<unsigned>(r * kRowBytes + ((ch ^ (r & 7)) << 4));
+}
+
 template <bool kCluster>
 __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
@@ -128,16 +181,15 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnPar
     return;
   }
   const int splits = p.splits, tile = p.tile;
-  const int group = p.heads / p.kv_heads, g4 = group4(group);
+  const int group = p.heads / p.kv_heads;
   const SmemLayout L = layout_for(tile, group, splits, !kCluster);
   unsigned char* ks = smem + L.ks;
   unsigned char* vs = smem + L.vs;
-  float* qs = reinterpret_cast<float*>(smem + L.qs);
-  float* sc = reinterpret_cast<float*>(smem + L.sc);
   float* red = reinterpret_cast<float*>(smem + L.red);
   float* part = reinterpret_cast<float*>(smem + L.part);
   float* ml = reinterpret_cast<float*>(smem + L.ml);
-  const unsigned bar = smem_addr(smem + L.bar);
+  float* wmax = reinterpret_cast<float*>(smem + L.stats);  // [warp][16 head rows]
+  float* wsum = wmax + kWarps * 16;                         // [warp][16 head rows]
 
   const int kvh = blockIdx.x / splits, c = blockIdx.x - kvh * splits;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -147,167 +199,196 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnPar
   const bool owns_new = len >= lo && len < lo + tile;             // the new token is local token ncache
   const int n = ncache + (owns_new ? 1 : 0);
 
-  // ---- 1. staging
-  if (tid == 0) {
-    mbar_init(bar, 1);
-    fence_mbar_init();
-    if (ncache > 0) {
-      const unsigned bytes = static_cast<unsigned>(ncache) * kRowBytes;
-      mbar_arrive_expect_tx(bar, bytes);
-      bulk_g2s(smem_addr(vs), p.vc + base + static_cast<size_t>(lo) * kHD, bytes, bar);
-    }
-  }
-  {  // K: eight 16-byte loads in flight per thread, then the swizzled stores
-    const uint4* src = reinterpret_cast<const uint4*>(p.kc + base + static_cast<size_t>(lo) * kHD);
+  const int tpw = p.tpw, rows = kWarps * tpw;
+
+  // ---- 1. staging: K and V rows by coalesced 16-byte loads (sixteen in flight per
+  // thread) into swizzled tiles; rows [n, rows) of V are zeroed (p = 0 there, and
+  // 0 * garbage could be NaN); the new token's row goes to the cache and the tiles.
+  {
+    const uint4* ksrc = reinterpret_cast<const uint4*>(p.kc + base + static_cast<size_t>(lo) * kHD);
+    const uint4* vsrc = reinterpret_cast<const uint4*>(p.vc + base + static_cast<size_t>(lo) * kHD);
     const int total = ncache * 8;
     for (int b = 0; b < total; b += 8 * kAttnThreads) {
-      uint4 buf[8];
+      uint4 kb[8], vb[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int i = b + u * kAttnThreads + tid;
-        if (i < total) buf[u] = __ldg(src + i);
+        if (i < total) {
+          kb[u] = __ldg(ksrc + i);
+          vb[u] = __ldg(vsrc + i);
+        }
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         const int i = b + u * kAttnThreads + tid;
         if (i < total) {
-          const int r = i >> 3, ch = i & 7;
-          *reinterpret_cast<uint4*>(ks + r * kRowBytes + ((ch ^ (r & 7)) << 4)) = buf[u];
+          const unsigned off = swz(i >> 3, i & 7);
+          *reinterpret_cast<uint4*>(ks + off) = kb[u];
+          *reinterpret_cast<uint4*>(vs + off) = vb[u];
         }
       }
     }
+    for (int i = n * 8 + tid; i < rows * 8; i += kAttnThreads)
+      *reinterpret_cast<uint4*>(vs + swz(i >> 3, i & 7)) = make_uint4(0u, 0u, 0u, 0u);
   }
-  if (owns_new && tid < 16) {  // append: 8 x 16 bytes of K, 8 of V, to the cache and to the tile
+  if (owns_new && tid < 16) {  // append: 8 x 16 bytes of K, 8 of V, to the cache and to the tiles
     const int ch = tid & 7;
     const bool is_v = tid >= 8;
     const uint4 v = __ldg(reinterpret_cast<const uint4*>((is_v ? p.v_new : p.k_new) + kvh * kHD) + ch);
     reinterpret_cast<uint4*>((is_v ? p.vc : p.kc) + base + static_cast<size_t>(len) * kHD)[ch] = v;
-    if (is_v)
-      reinterpret_cast<uint4*>(vs + ncache * kRowBytes)[ch] = v;
-    else
-      *reinterpret_cast<uint4*>(ks + ncache * kRowBytes + ((ch ^ (ncache & 7)) << 4)) = v;
+    *reinterpret_cast<uint4*>((is_v ? vs : ks) + swz(ncache, ch)) = v;
   }
-  for (int i = tid; i < g4 * kHD; i += kAttnThreads) {
-    const int h = i / kHD;
-    qs[i] = h < group ? __fmul_rn(bf16lo(p.q[(kvh * group) * kHD + i]), p.scale) : 0.0f;
+  // q as the A fragments of the four 16-dimension steps: head rows g and g + 8
+  // (zero beyond the group), dimensions 16 kk + 2 t (+ 8).
+  const int g = lane >> 2, t4 = lane & 3;
+  unsigned qa[4][4];
+  {
+    const unsigned* q0 = reinterpret_cast<const unsigned*>(p.q + (kvh * group + g) * kHD);
+    const unsigned* q1 = reinterpret_cast<const unsigned*>(p.q + (kvh * group + g + 8) * kHD);
+    const bool r0 = g < group, r1 = g + 8 < group;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      qa[kk][0] = r0 ? __ldg(q0 + 8 * kk + t4) : 0u;
+      qa[kk][1] = r1 ? __ldg(q1 + 8 * kk + t4) : 0u;
+      qa[kk][2] = r0 ? __ldg(q0 + 8 * kk + 4 + t4) : 0u;
+      qa[kk][3] = r1 ? __ldg(q1 + 8 * kk + 4 + t4) : 0u;
+    }
   }
   __syncthreads();
 
-  // ---- 2. scores s[j][h] = (q_h * scale) . k_j
-  for (int j = tid; j < n; j += kAttnThreads) {
-    const unsigned char* krow = ks + j * kRowBytes;
-    for (int hb = 0; hb < g4; hb += 4) {
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  // ---- 2. scores S = (Q K^T) * scale on the tensor cores: warp w takes tokens
+  // [w * tpw, (w + 1) * tpw) in 8-token tiles; tokens >= n are masked to -inf.
+  const int j0w = warp * tpw;
+  const bool active = j0w < n;  // warp-uniform
+  const int ntile = tpw / 8;
+  const unsigned ks0 = smem_addr(ks), vs0 = smem_addr(vs);
+  float s[8][4];
+  float mx0 = kNegInf, mx1 = kNegInf;
+  if (active) {
 #pragma unroll
-      for (int i = 0; i < kHD / 8; ++i) {
-        const uint4 kv = *reinterpret_cast<const uint4*>(krow + ((i ^ (j & 7)) << 4));
-        const float k8[8] = {bf16lo(kv.x), bf16hi(kv.x), bf16lo(kv.y), bf16hi(kv.y),
-                             bf16lo(kv.z), bf16hi(kv.z), bf16lo(kv.w), bf16hi(kv.w)};
+    for (int tt = 0; tt < 8; ++tt) {
+      if (tt < ntile) {
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const int row = j0w + 8 * tt + (lane & 7);
 #pragma unroll
-        for (int hh = 0; hh < 4; ++hh) {
-          const float4 q0 = *reinterpret_cast<const float4*>(qs + (hb + hh) * kHD + 8 * i);
-          const float4 q1 = *reinterpret_cast<const float4*>(qs + (hb + hh) * kHD + 8 * i + 4);
-          float a = acc[hh];
-          a = __fmaf_rn(q0.x, k8[0], a);
-          a = __fmaf_rn(q0.y, k8[1], a);
-          a = __fmaf_rn(q0.z, k8[2], a);
-          a = __fmaf_rn(q0.w, k8[3], a);
-          a = __fmaf_rn(q1.x, k8[4], a);
-          a = __fmaf_rn(q1.y, k8[5], a);
-          a = __fmaf_rn(q1.z, k8[6], a);
-          a = __fmaf_rn(q1.w, k8[7], a);
-          acc[hh] = a;
+        for (int kk = 0; kk < 4; kk += 2) {
+          unsigned b[4];  // chunks 2kk .. 2kk + 3 of 8 token rows: B fragments of steps kk, kk + 1
+          ldsm_x4(ks0 + swz(row, 2 * kk + (lane >> 3)), b);
+          mma_bf16_16816(acc, qa[kk], b[0], b[1]);
+          mma_bf16_16816(acc, qa[kk + 1], b[2], b[3]);
         }
+        const int col = j0w + 8 * tt + 2 * t4;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[tt][e] = col + (e & 1) < n ? __fmul_rn(acc[e], p.scale) : kNegInf;
+        mx0 = fmaxf(mx0, fmaxf(s[tt][0], s[tt][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[tt][2], s[tt][3]));
       }
-      *reinterpret_cast<float4*>(sc + j * g4 + hb) = make_float4(acc[0], acc[1], acc[2], acc[3]);
     }
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  if (t4 == 0) {
+    wmax[warp * 16 + g] = mx0;
+    wmax[warp * 16 + g + 8] = mx1;
   }
   __syncthreads();
 
-  // ---- 3. softmax partials; p replaces s (padded heads stay finite: p = 0)
-  for (int h = warp; h < g4; h += kWarps) {
-    if (h >= group) {
-      for (int j = lane; j < n; j += 32) sc[j * g4 + h] = 0.0f;
-      continue;
-    }
-    float m = __int_as_float(0xff800000u);
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[j * g4 + h]);
-    m = warp_max(m);
-    float l = 0.0f;
-    for (int j = lane; j < n; j += 32) {
-      const float e = __expf(__fsub_rn(sc[j * g4 + h], m));
-      sc[j * g4 + h] = e;
-      l = __fadd_rn(l, e);
-    }
-    l = warp_allsum(l);
-    if (lane == 0) {
-      ml[2 * h] = m;
-      ml[2 * h + 1] = l;
-    }
+  // ---- 3. p = exp(s - m) in registers; per-warp row sums
+  float m0 = kNegInf, m1 = kNegInf;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) {
+    m0 = fmaxf(m0, wmax[w * 16 + g]);
+    m1 = fmaxf(m1, wmax[w * 16 + g + 8]);
   }
-  if (ncache > 0 && !mbar_wait(bar, 0)) record_status(p.status, kStatusMbarTimeout);
-  __syncthreads();
-
-  // ---- 4. o[h][d] = sum_j p[j][h] v[j][d]; thread (dc = 8-dim chunk, cls = token class)
-  const int dc = tid & 7, cls = tid >> 3;
-  for (int hb = 0; hb < g4; hb += 4) {
-    float acc[4][8];
+  float l0 = 0.0f, l1 = 0.0f;
+  float o[8][4];
 #pragma unroll
-    for (int hh = 0; hh < 4; ++hh)
+  for (int nd = 0; nd < 8; ++nd)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[hh][e] = 0.0f;
-#pragma unroll 2
-    for (int j = cls; j < n; j += kAttnThreads / 8) {
-      const uint4 v = *reinterpret_cast<const uint4*>(vs + j * kRowBytes + dc * 16);
-      const float4 pj = *reinterpret_cast<const float4*>(sc + j * g4 + hb);
-      const float v8[8] = {bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y),
-                           bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w)};
-      const float pp[4] = {pj.x, pj.y, pj.z, pj.w};
+    for (int e = 0; e < 4; ++e) o[nd][e] = 0.0f;
+  if (active) {
 #pragma unroll
-      for (int hh = 0; hh < 4; ++hh)
+    for (int tt = 0; tt < 8; ++tt) {
+      if (tt < ntile) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[hh][e] = __fmaf_rn(pp[hh], v8[e], acc[hh][e]);
-    }
-    // Token classes of one warp: lanes dc, dc + 8, dc + 16, dc + 24.
-#pragma unroll
-    for (int hh = 0; hh < 4; ++hh)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        float a = acc[hh][e];
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 8));
-        a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 16));
-        acc[hh][e] = a;
-      }
-    if (lane < 8) {
-#pragma unroll
-      for (int hh = 0; hh < 4; ++hh) {
-        float4* dst = reinterpret_cast<float4*>(red + (warp * 4 + hh) * kHD + dc * 8);
-        dst[0] = make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
-        dst[1] = make_float4(acc[hh][4], acc[hh][5], acc[hh][6], acc[hh][7]);
+        for (int e = 0; e < 4; ++e) {
+          const float m = e < 2 ? m0 : m1;
+          s[tt][e] = s[tt][e] == kNegInf ? 0.0f : __expf(__fsub_rn(s[tt][e], m));
+        }
+        l0 = __fadd_rn(l0, __fadd_rn(s[tt][0], s[tt][1]));
+        l1 = __fadd_rn(l1, __fadd_rn(s[tt][2], s[tt][3]));
       }
     }
-    __syncthreads();
-    {  // thread (hh, d): warps summed in order
-      const int hh = tid >> 6, d = tid & 63, h = hb + hh;
-      float o = 0.0f;
+    // ---- 4. O = P V on the tensor cores: P (16 heads x 16 tokens) as hi + lo
+    // BF16 A fragments straight from the score accumulators; V B fragments by
+    // transposing loads of the swizzled tile.
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) o = __fadd_rn(o, red[(w * 4 + hh) * kHD + d]);
-      if (h < group) {
-        if (splits == 1) {
-          p.out[(kvh * group + h) * kHD + d] = rne_bf16(__fdiv_rn(o, ml[2 * h + 1]));
-        } else {
-          float* rec = kCluster ? part + h * kRecord
-                                : p.scratch + (static_cast<size_t>(kvh * group + h) * splits + c) * kRecord;
-          rec[2 + d] = o;
-          if (d == 0) {
-            const bool any = n > 0;
-            rec[0] = any ? ml[2 * h] : __int_as_float(0xff800000u);
-            rec[1] = any ? ml[2 * h + 1] : 0.0f;
-          }
+    for (int kt = 0; kt < 4; ++kt) {
+      if (2 * kt < ntile) {
+        unsigned ahi[4], alo[4];
+        split_bf16x2(s[2 * kt][0], s[2 * kt][1], ahi[0], alo[0]);
+        split_bf16x2(s[2 * kt][2], s[2 * kt][3], ahi[1], alo[1]);
+        split_bf16x2(s[2 * kt + 1][0], s[2 * kt + 1][1], ahi[2], alo[2]);
+        split_bf16x2(s[2 * kt + 1][2], s[2 * kt + 1][3], ahi[3], alo[3]);
+        const int mi = lane >> 3;
+        const int row = j0w + 16 * kt + (lane & 7) + ((mi & 1) << 3);
+#pragma unroll
+        for (int nd = 0; nd < 8; nd += 2) {
+          unsigned b[4];  // dims 8 nd .. 8 nd + 15: B fragments of output tiles nd, nd + 1
+          ldsm_x4_trans(vs0 + swz(row, nd + (mi >> 1)), b);
+          mma_bf16_16816(o[nd], ahi, b[0], b[1]);
+          mma_bf16_16816(o[nd], alo, b[0], b[1]);
+          mma_bf16_16816(o[nd + 1], ahi, b[2], b[3]);
+          mma_bf16_16816(o[nd + 1], alo, b[2], b[3]);
         }
       }
     }
-    __syncthreads();
+  }
+  l0 = __fadd_rn(l0, __shfl_xor_sync(0xffffffffu, l0, 1));
+  l0 = __fadd_rn(l0, __shfl_xor_sync(0xffffffffu, l0, 2));
+  l1 = __fadd_rn(l1, __shfl_xor_sync(0xffffffffu, l1, 1));
+  l1 = __fadd_rn(l1, __shfl_xor_sync(0xffffffffu, l1, 2));
+  if (t4 == 0) {
+    wsum[warp * 16 + g] = l0;
+    wsum[warp * 16 + g + 8] = l1;
+  }
+#pragma unroll
+  for (int nd = 0; nd < 8; ++nd) {
+    float* r0 = red + (warp * 16 + g) * kRedStride + 8 * nd + 2 * t4;
+    *reinterpret_cast<float2*>(r0) = make_float2(o[nd][0], o[nd][1]);
+    *reinterpret_cast<float2*>(r0 + 8 * kRedStride) = make_float2(o[nd][2], o[nd][3]);
+  }
+  __syncthreads();
+  if (tid < group) {  // m and l per head row, warps summed in order
+    float m = kNegInf, l = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      m = fmaxf(m, wmax[w * 16 + tid]);
+      l = __fadd_rn(l, wsum[w * 16 + tid]);
+    }
+    ml[2 * tid] = m;
+    ml[2 * tid + 1] = l;
+  }
+  __syncthreads();
+  for (int it = tid; it < group * kHD; it += kAttnThreads) {  // o per (head, dim): warps in order
+    const int h = it / kHD, d = it - h * kHD;
+    float acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) acc = __fadd_rn(acc, red[(w * 16 + h) * kRedStride + d]);
+    if (splits == 1) {
+      p.out[(kvh * group + h) * kHD + d] = rne_bf16(__fdiv_rn(acc, ml[2 * h + 1]));
+    } else {
+      float* rec = kCluster ? part + h * kRecord
+                            : p.scratch + (static_cast<size_t>(kvh * group + h) * splits + c) * kRecord;
+      rec[2 + d] = acc;
+      if (d == 0) {
+        const bool any = n > 0;
+        rec[0] = any ? ml[2 * h] : kNegInf;
+        rec[1] = any ? ml[2 * h + 1] : 0.0f;
+      }
+    }
   }
   if (splits == 1) return;
 
@@ -345,7 +426,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnPar
     }
     cluster_sync_all();  // no CTA leaves while another reads its shared memory
   } else {
-    unsigned* s_ticket = reinterpret_cast<unsigned*>(smem + L.bar + 8);
+    unsigned* s_ticket = reinterpret_cast<unsigned*>(smem + L.tk);
     float* wts = reinterpret_cast<float*>(smem + L.wts);
     __threadfence();
     __syncthreads();
@@ -427,7 +508,7 @@ AttnPlan plan_for(int span, int kv_heads, const AttnDevice& dev) {
   AttnPlan plan{};
   const int csplits = splits < dev.cluster_max ? splits : dev.cluster_max;
   int tile = ((span + csplits - 1) / csplits + kMinTile - 1) / kMinTile * kMinTile;
-  if (tile <= kMaxTile) {
+  if (KLAB_ATTN_CLUSTER && tile <= kMaxTile) {
     plan.tile = tile;
     plan.splits = (span + tile - 1) / tile;
     plan.cluster = true;
@@ -503,7 +584,8 @@ KLAB_API int klab_decode_attention(const void* q, const void* k_new, const void*
   if (prep) return prep;
   const AttnPlan plan = plan_for(len_ptr ? max_len : len + 1, kv_heads, g_attn_dev[dev]);
   if (static_cast<long long>(heads) * plan.splits * kRecord > scratch_floats) return KLAB_E_INVALID;
-  const size_t smem = layout_for(plan.tile, heads / kv_heads, plan.splits, !plan.cluster).total;
+  size_t smem = layout_for(plan.tile, heads / kv_heads, plan.splits, !plan.cluster).total;
+  if (smem < KLAB_ATTN_SMEM_FLOOR) smem = KLAB_ATTN_SMEM_FLOOR;
   if (smem > kMaxSmem) return KLAB_E_SHAPE;
   AttnParams p{};
   p.q = static_cast<const unsigned short*>(q);
@@ -522,6 +604,7 @@ KLAB_API int klab_decode_attention(const void* q, const void* k_new, const void*
   p.kv_heads = kv_heads;
   p.splits = plan.splits;
   p.tile = plan.tile;
+  p.tpw = tokens_per_warp(plan.tile);
   p.scale = scale;
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute attr[2];
