@@ -42,7 +42,8 @@ def check(out, q, kn, vn, K, V, L, h, kvh):
 
 
 @pytest.mark.parametrize("h,kvh,L,cap", [(9, 3, 0, 512), (14, 2, 7, 512), (32, 4, 300, 512),
-                                         (32, 8, 4095, 4096), (16, 1, 63, 128), (16, 16, 64, 128)])
+                                         (32, 8, 4095, 4096), (16, 1, 63, 128), (16, 16, 64, 128),
+                                         (32, 8, 700, 1024), (48, 4, 256, 512)])
 def test_matches_oracle_and_appends(h, kvh, L, cap):
     from klab_b200.decode_attn import decode_attention
 
