@@ -9,9 +9,9 @@
 // length is read from device memory) is cut into `splits` tiles of `tile` tokens
 // (a multiple of 64, at most 512). CTA (kv head, split) serves every query head
 // of its group, so each K/V row crosses HBM once:
-//   1. K and V rows are loaded with coalesced 16-byte loads (sixteen in flight per
-//      thread) and stored XOR-swizzled (chunk i of row r at chunk i ^ (r mod 8)),
-//      which keeps the fragment loads below conflict-free. The CTA whose tile
+//   1. K and V rows are copied with coalesced 16-byte cp.async into XOR-swizzled
+//      tiles (chunk i of row r at chunk i ^ (r mod 8)), which keeps the fragment
+//      loads below conflict-free; V's copies land while the scores run. The CTA whose tile
 //      holds position `len` writes the new K/V row into the cache and its tiles.
 //   2. Scores on the tensor cores (mma.sync m16n8k16, BF16 in, FP32 out): the
 //      group's query heads (at most 16) are the 16 rows of the A fragment, loaded
@@ -204,33 +204,23 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnPar
 
   const int tpw = p.tpw, rows = kWarps * tpw;
 
-  // ---- 1. staging: K and V rows by coalesced 16-byte loads (sixteen in flight per
-  // thread) into swizzled tiles; rows [n, rows) of V are zeroed (p = 0 there, and
-  // 0 * garbage could be NaN); the new token's row goes to the cache and the tiles.
+  // ---- 1. staging: K and V rows by 16-byte cp.async copies (coalesced, straight
+  // into the swizzled tiles, every copy of the tile in flight at once; K and V in
+  // separate groups); rows [n, rows) of V are zeroed (p = 0 there, and 0 * garbage
+  // could be NaN); the new token's row goes to the cache and the tiles.
   {
     const uint4* ksrc = reinterpret_cast<const uint4*>(p.kc + base + static_cast<size_t>(lo) * kHD);
     const uint4* vsrc = reinterpret_cast<const uint4*>(p.vc + base + static_cast<size_t>(lo) * kHD);
     const int total = ncache * 8;
-    for (int b = 0; b < total; b += 8 * kAttnThreads) {
-      uint4 kb[8], vb[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = b + u * kAttnThreads + tid;
-        if (i < total) {
-          kb[u] = __ldg(ksrc + i);
-          vb[u] = __ldg(vsrc + i);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int i = b + u * kAttnThreads + tid;
-        if (i < total) {
-          const unsigned off = swz(i >> 3, i & 7);
-          *reinterpret_cast<uint4*>(ks + off) = kb[u];
-          *reinterpret_cast<uint4*>(vs + off) = vb[u];
-        }
-      }
-    }
+    const unsigned ks_s = smem_addr(ks), vs_s = smem_addr(vs);
+    for (int i = tid; i < total; i += kAttnThreads)  // K first: the scores wait for it alone
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(ks_s + swz(i >> 3, i & 7)), "l"(ksrc + i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    for (int i = tid; i < total; i += kAttnThreads)  // V lands while the scores run
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(vs_s + swz(i >> 3, i & 7)), "l"(vsrc + i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
     for (int i = n * 8 + tid; i < rows * 8; i += kAttnThreads)
       *reinterpret_cast<uint4*>(vs + swz(i >> 3, i & 7)) = make_uint4(0u, 0u, 0u, 0u);
   }
@@ -257,6 +247,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnPar
       qa[kk][3] = r1 ? __ldg(q1 + 8 * kk + 4 + t4) : 0u;
     }
   }
+  asm volatile("cp.async.wait_group 1;" ::: "memory");  // this thread's K copies
   __syncthreads();
 
   // ---- 2. scores S = (Q K^T) * scale on the tensor cores: warp w takes tokens
@@ -296,6 +287,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnPar
     wmax[warp * 16 + g] = mx0;
     wmax[warp * 16 + g + 8] = mx1;
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // this thread's V copies
   __syncthreads();
 
   // ---- 3. p = exp(s - m) in registers; per-warp row sums
