@@ -61,9 +61,9 @@ def test_sharded_chain_matches_single_rank():
     x_bits = og.normal_bf16_bits(7, (1, SHAPE["hidden"]), 1.0)
     single = {}
     _run(0, 1, _free_port(), x_bits, single)
-    with mp.Manager() as manager:
+    ctx = mp.get_context("spawn")  # the manager too: no fork of this multi-threaded process
+    with ctx.Manager() as manager:
         shared = manager.dict()
-        ctx = mp.get_context("spawn")
         port = _free_port()
         procs = [ctx.Process(target=_run, args=(r, 2, port, x_bits, shared)) for r in range(2)]
         for p in procs:
