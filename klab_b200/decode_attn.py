@@ -23,9 +23,16 @@ from .decode_ops import add_rmsnorm, silu_mul  # noqa: F401  (same module surfac
 
 HD = 64
 CHUNK = 64
+SOURCE = "klab_b200/csrc/decode_attn.cu"  # the reference names its NVRTC source here
 _KERNELS = ("decode_attn_bf16", "decode_attn_v2_bf16", "decode_attn_v3_bf16", "decode_attn_v4_bf16",
             "decode_attn_v5_bf16")
 _work = {}
+
+
+def module():
+    """The native module serving these kernels on the current device (the reference's module()
+    returns its NVRTC-compiled CudaModule, decode_attn.py:12-17)."""
+    return get_module()
 
 
 def _workspace(device, heads, kv_heads, max_len):

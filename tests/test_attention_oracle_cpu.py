@@ -31,3 +31,12 @@ def test_single_token_returns_new_value():
     K = V = np.zeros((1, 4, 64), dtype=np.uint16)
     got = oa.decode_attention64(q, kn, vn, K, V, 0, 2, 1)
     np.testing.assert_array_equal(got.reshape(2, 64), np.stack([bf16_values(vn)] * 2))
+
+
+def test_decode_attn_module_surface():
+    """The mirror keeps the reference module's public names (decode_attn.py:7-107)."""
+    import klab_b200.decode_attn as d
+
+    for name in ("module", "decode_attention", "decode_attention_dynamic", "add_rmsnorm", "silu_mul"):
+        assert callable(getattr(d, name)), name
+    assert d.SOURCE.endswith("decode_attn.cu")
