@@ -36,7 +36,9 @@
 // device status word (kStatusBadLength).
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdint>
+#include <mutex>
 
 #include "common.cuh"
 #include "klab_b200.h"
@@ -483,7 +485,7 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attn_kernel(const AttnPar
 }
 
 struct AttnDevice {
-  bool ready;
+  std::atomic<bool> ready;
   int sms;
   int cluster_max;  // largest cluster the cluster mode may use on this device
 };
@@ -521,9 +523,15 @@ AttnPlan plan_for(int span, int kv_heads, const AttnDevice& dev) {
   return plan;
 }
 
+std::mutex g_attn_mutex;
+
+// Once per device (the caller's device is current): kernel attributes, SM count and
+// the largest usable cluster. Guarded so concurrent first calls do it once.
 int prepare_device(int dev) {
   AttnDevice& d = g_attn_dev[dev];
-  if (d.ready) return 0;
+  if (d.ready.load(std::memory_order_acquire)) return 0;
+  std::lock_guard<std::mutex> lock(g_attn_mutex);
+  if (d.ready.load(std::memory_order_relaxed)) return 0;
   cudaError_t err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
   if (err != cudaSuccess) return err;
   err = cudaFuncSetAttribute(decode_attn_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -552,7 +560,7 @@ int prepare_device(int dev) {
       d.cluster_max = kMaxClusterSplits;
   }
   (void)cudaGetLastError();
-  d.ready = true;
+  d.ready.store(true, std::memory_order_release);
   return 0;
 }
 
