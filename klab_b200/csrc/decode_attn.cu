@@ -54,7 +54,7 @@ constexpr int kRowBytes = kHD * 2;  // one BF16 K or V row
 #endif
 constexpr int kMinTile = KLAB_ATTN_MIN_TILE;
 #ifndef KLAB_ATTN_SINGLE_SPAN
-#define KLAB_ATTN_SINGLE_SPAN 256  // spans up to this many tokens run as one tile per kv head (no merge)
+#define KLAB_ATTN_SINGLE_SPAN 384  // spans up to this many tokens run as one tile per kv head (no merge)
 #endif
 #ifndef KLAB_ATTN_CLUSTER
 #define KLAB_ATTN_CLUSTER 1  // 1: merge over a thread-block cluster when one covers the span
@@ -491,12 +491,13 @@ struct AttnDevice {
 };
 AttnDevice g_attn_dev[64];
 
-// Short spans (<= 256 tokens) run as one tile per kv head with no merge. Longer
+// Short spans (<= 384 tokens) run as one tile per kv head with no merge. Longer
 // spans: tiles of at least 128 tokens, cluster mode whenever one cluster of
 // `splits` CTAs covers the span with tiles of at most 512 tokens; the split count
-// aims at about two CTAs per SM. (Measured on B200 at 32/8 heads: one 256-token
-// tile 4.7 us vs four 64-token tiles 5.4 us; 1024 tokens as 8 x 128 6.2 us vs
-// 16 x 64 6.8 us.)
+// aims at about two CTAs per SM. (Measured on B200 at 32/8 heads: 256 tokens as one
+// tile 4.7 us vs four 64-token tiles 5.4 us; 384 tokens as one tile 4.9 us vs three
+// 128-token tiles 5.2 us, but 512 tokens as one tile 5.5 us vs four 5.2 us; 1024
+// tokens as 8 x 128 6.2 us vs 16 x 64 6.8 us.)
 struct AttnPlan {
   int splits, tile;
   bool cluster;
