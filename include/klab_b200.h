@@ -65,6 +65,7 @@ extern "C" {
 #define KLAB_L2_HINT 0
 #define KLAB_L2_HINT_LAST 1
 #define KLAB_L2_LOAD 2
+#define KLAB_L2_BULK 3 /* this library's own: cp.async.bulk.prefetch.L2, `stride` = bytes per request */
 
 /* Error codes. -1000..-1002 keep the meaning of the reference driver ABI. */
 #define KLAB_E_DRIVER (-1000)      /* CUDA driver or a required symbol not loadable */
@@ -281,14 +282,17 @@ KLAB_API int klab_decode_attention(const void* q, const void* k_new, const void*
 
 /* Fused: the projection out[M,N] = xn . W^T (BF16 W [N,K], BF16 out) with xn computed while
  * x is staged, as klab_add_rmsnorm would (x_out, when not null, gets RNE(res + y)); bit-identical
- * to klab_add_rmsnorm followed by klab_raw_linear. K % 8 == 0. No counterpart kernel in the
+ * to klab_add_rmsnorm followed by klab_raw_linear. K % 8 == 0. x_out and out must not overlap res,
+ * y, norm_weight or each other (no in-place residual update: every CTA re-reads res and y while
+ * another writes x_out); an overlap returns KLAB_E_INVALID. No counterpart kernel in the
  * reference: it fuses its add_rmsnorm_bf16 into the next projection (the "prologue fusion"
  * named beside kernels.cu:168-222 and decode_attn.cu:473). */
 KLAB_API int klab_add_rmsnorm_linear(const void* res, const void* y, const void* norm_weight, float eps,
                                      const void* w, void* out, void* x_out, int m, int n, int k, void* workspace,
                                      size_t workspace_bytes, void* stream);
 /* Fused: out[M,N] = silu_mul(gu) . W^T with gu [M, 2*inter], W [N, inter]; bit-identical to
- * klab_silu_mul followed by klab_raw_linear. inter % 8 == 0. No counterpart kernel in the
+ * klab_silu_mul followed by klab_raw_linear. inter % 8 == 0; out must not overlap gu
+ * (KLAB_E_INVALID). No counterpart kernel in the
  * reference (fuses its silu_mul_bf16, decode_attn.cu:513-527, into the down projection). */
 KLAB_API int klab_silu_mul_linear(const void* gu, const void* w, void* out, int m, int n, int inter,
                                   void* workspace, size_t workspace_bytes, void* stream);
@@ -375,7 +379,8 @@ KLAB_API int klab_cbf16_unpack_host(const uint8_t* payload, size_t payload_bytes
  * threads, one request per `stride` bytes; never writes. sink: a device word
  * (never written in practice). Replaces l2prefetch.prefetch
  * (research/l2-prefetch/src/l2prefetch.py:27-35; kernels l2_hint / l2_hint_last /
- * l2_load, prefetch_kernels.cu:3-25). */
+ * l2_load, prefetch_kernels.cu:3-25). KLAB_L2_BULK has no counterpart in the reference: each
+ * thread hands `stride` bytes (16 B .. 64 KiB) at a time to the bulk-copy engine. */
 KLAB_API int klab_l2_prefetch(const void* p, long long bytes, int blocks, int threads, int stride, int kind,
                      unsigned* sink, void* stream);
 

@@ -404,6 +404,12 @@ int run_gemv(int wfmt, int xdt, const void* x, int ldx, const void* w, const voi
   return run_gemv_multi(wfmt, xdt, x, ldx, 1, ws_, as_, gscale, os_, ldo_, n_, out_dt, m, k, ws, ws_bytes, stream);
 }
 
+// Byte ranges [a, a + na) and [b, b + nb) share at least one byte.
+bool overlaps(const void* a, size_t na, const void* b, size_t nb) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  return pa < pb + nb && pb < pa + na;
+}
+
 }  // namespace
 }  // namespace klab
 
@@ -429,6 +435,14 @@ int klab_add_rmsnorm_linear(const void* res, const void* y, const void* norm_wei
                             void* stream) {
   if (!res || !y || !norm_weight || !w || !out || m <= 0 || n <= 0 || k <= 0 || !(eps > 0.0f)) return KLAB_E_INVALID;
   if (k % 8) return KLAB_E_SHAPE;
+  // Every CTA re-reads res and y while it stages x, and column 0 of the grid writes x_out: an x_out
+  // (or out) that overlaps what the launch reads would feed updated values to later CTAs.
+  const size_t act = size_t(m) * size_t(k) * 2, outb = size_t(m) * size_t(n) * 2;
+  if (x_out && (overlaps(x_out, act, res, act) || overlaps(x_out, act, y, act) ||
+                overlaps(x_out, act, norm_weight, size_t(k) * 2) || overlaps(x_out, act, out, outb)))
+    return KLAB_E_INVALID;
+  if (overlaps(out, outb, res, act) || overlaps(out, outb, y, act) || overlaps(out, outb, norm_weight, size_t(k) * 2))
+    return KLAB_E_INVALID;
   const uintptr_t mis = reinterpret_cast<uintptr_t>(res) | reinterpret_cast<uintptr_t>(y) |
                         reinterpret_cast<uintptr_t>(norm_weight) | reinterpret_cast<uintptr_t>(x_out);
   if (mis & 3) return KLAB_E_ALIGN;
@@ -453,6 +467,7 @@ int klab_silu_mul_linear(const void* gu, const void* w, void* out, int m, int n,
                          size_t workspace_bytes, void* stream) {
   if (!gu || !w || !out || m <= 0 || n <= 0 || inter <= 0) return KLAB_E_INVALID;
   if (inter % 8) return KLAB_E_SHAPE;
+  if (overlaps(out, size_t(m) * size_t(n) * 2, gu, size_t(m) * size_t(inter) * 4)) return KLAB_E_INVALID;
   if (reinterpret_cast<uintptr_t>(gu) & 3) return KLAB_E_ALIGN;
   Prologue pr = {};
   pr.op = PRO_SILU_MUL;
@@ -722,7 +737,8 @@ int klab_fp4_dequantize(const uint8_t* packed, const void* scales, int scale_kin
 int klab_l2_prefetch(const void* p, long long bytes, int blocks, int threads, int stride, int kind, unsigned* sink,
                      void* stream) {
   if (!p || bytes < 0 || blocks <= 0 || threads <= 0 || threads > 1024 || stride <= 0) return KLAB_E_INVALID;
-  if (kind != KLAB_L2_HINT && kind != KLAB_L2_HINT_LAST && kind != KLAB_L2_LOAD) return KLAB_E_UNSUPPORTED;
+  if (kind != KLAB_L2_HINT && kind != KLAB_L2_HINT_LAST && kind != KLAB_L2_LOAD && kind != KLAB_L2_BULK)
+    return KLAB_E_UNSUPPORTED;
   if (kind == KLAB_L2_LOAD && !sink) return KLAB_E_INVALID;
   return launch_l2_prefetch(p, bytes, blocks, stride, threads, kind, sink, static_cast<cudaStream_t>(stream));
 }

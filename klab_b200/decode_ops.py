@@ -67,6 +67,12 @@ def silu_mul(gu):
     return out
 
 
+def _overlap(a, b):
+    """True when two tensors' storage byte ranges intersect."""
+    pa, pb = a.data_ptr(), b.data_ptr()
+    return pa < pb + b.numel() * b.element_size() and pb < pa + a.numel() * a.element_size()
+
+
 def _projection_out(out, m, n, like):
     if out is None:
         return torch.empty((m, n), device=like.device, dtype=torch.bfloat16)
@@ -95,6 +101,14 @@ def add_rmsnorm_linear(res, y, norm_weight, w, eps=1e-6, out=None, x_out=None):
         _check_bf16(x_out)
         if x_out.shape != res.shape:
             raise ValueError("x_out shape mismatch")
+    # Every CTA re-reads res and y while it stages x and one column of CTAs writes x_out, so an
+    # in-place residual update (x_out aliasing res or y) would feed updated values to later CTAs.
+    written = [out] + ([] if x_out is False else [x_out])
+    for dst in written:
+        if any(_overlap(dst, src) for src in (res, y, norm_weight)):
+            raise ValueError("x_out and out must not overlap res, y or norm_weight")
+    if x_out is not False and _overlap(x_out, out):
+        raise ValueError("x_out and out must not overlap")
     stream = torch.cuda.current_stream(res.device)
     ws_ptr, ws_bytes = _native.workspace_for(_native.W_BF16, m, n, k, res.device.index, stream)
     with torch.cuda.device(res.device):
@@ -118,6 +132,8 @@ def silu_mul_linear(gu, w, out=None):
         raise ValueError("inter must be a multiple of 8")
     get_module(gu.device)
     out = _projection_out(out, m, n, gu)
+    if _overlap(out, gu):
+        raise ValueError("out must not overlap gu")
     stream = torch.cuda.current_stream(gu.device)
     ws_ptr, ws_bytes = _native.workspace_for(_native.W_BF16, m, n, inter, gu.device.index, stream)
     with torch.cuda.device(gu.device):

@@ -92,6 +92,14 @@ def test_invalid_arguments_rejected_before_any_device_work():
     assert lib.klab_add_rmsnorm_linear(fake, fake, fake, 1e-6, fake, fake, None, 1, 8, 60, None, 0, None) \
         == _native.E_SHAPE
     assert lib.klab_silu_mul_linear(fake, fake, fake, 1, 8, 60, None, 0, None) == _native.E_SHAPE
+    # Fused add+RMSNorm: an in-place residual update (x_out over res or y) or an out over the
+    # inputs is rejected before launch; the addresses are never dereferenced.
+    res, y, nw, w, out, xo = 1 << 20, 2 << 20, 3 << 20, 4 << 20, 5 << 20, 6 << 20
+    for bad in ((res, y, nw, w, out, res), (res, y, nw, w, out, y + 64), (res, y, nw, w, res, xo),
+                (res, y, nw, w, out, out)):
+        assert lib.klab_add_rmsnorm_linear(bad[0], bad[1], bad[2], 1e-6, bad[3], bad[4], bad[5], 2, 8, 64, None, 0,
+                                           None) == _native.E_INVALID, bad
+    assert lib.klab_silu_mul_linear(res, w, res + 128, 2, 8, 64, None, 0, None) == _native.E_INVALID
     assert lib.klab_decode_attention(fake, fake, fake, fake, fake, fake, fake, 1 << 20, fake, None, 0, 64, 34, 2,
                                      0.125, None) == _native.E_SHAPE  # 17 query heads per kv head
     assert lib.klab_decode_attention(fake, fake, fake, fake, fake, fake, fake, 1 << 20, fake, None, 64, 64, 8, 2,

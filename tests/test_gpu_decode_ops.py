@@ -133,3 +133,30 @@ def test_validation():
     with pytest.raises(ValueError):
         decode_ops.silu_mul_linear(torch.randn(2, 20, device="cuda").bfloat16(),
                                    torch.randn(4, 10, device="cuda").bfloat16())
+
+
+def test_fused_add_rmsnorm_linear_rejects_in_place_update(native):
+    """x_out over res or y (an in-place residual update) would let later CTAs read the
+    updated x; the Python layer raises ValueError and the C ABI returns KLAB_E_INVALID."""
+    from klab_b200 import decode_ops
+
+    m, k, n = 1, 1024, 64
+    res, y = torch.randn(m, k, device="cuda").bfloat16(), torch.randn(m, k, device="cuda").bfloat16()
+    g = torch.rand(k, device="cuda").bfloat16()
+    w = (torch.randn(n, k, device="cuda") * 0.02).bfloat16()
+    for x_out in (res, y):
+        with pytest.raises(ValueError):
+            decode_ops.add_rmsnorm_linear(res, y, g, w, x_out=x_out)
+    with pytest.raises(ValueError):
+        decode_ops.add_rmsnorm_linear(res, y, g, w, out=res[:, :n])
+    gu = torch.randn(m, 2 * k, device="cuda").bfloat16()
+    with pytest.raises(ValueError):
+        decode_ops.silu_mul_linear(gu, w, out=gu[:, :n])
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    stream = torch.cuda.current_stream().cuda_stream
+    rc = native.lib().klab_add_rmsnorm_linear(res.data_ptr(), y.data_ptr(), g.data_ptr(), 1e-6, w.data_ptr(),
+                                              out.data_ptr(), res.data_ptr(), m, n, k, None, 0, stream)
+    assert rc == native.E_INVALID
+    # the legal call still matches the standalone op followed by the projection
+    x, ref = decode_ops.add_rmsnorm_linear(res, y, g, w)
+    assert same_bits(x, res + y)
