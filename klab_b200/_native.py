@@ -23,7 +23,7 @@ PREFETCH_CUBIN = LIB_DIR / "prefetch_kernels.cubin"
 DT_BF16, DT_F16, DT_F32 = 0, 1, 2
 W_BF16, W_F16, W_F32, W_CBF16, W_I8_ROW, W_I8_G64, W_FP4_G32H, W_FP4_G16E, W_LF32, W_FP28 = range(10)
 FP4_E4M3_G16, FP4_F16_G32 = 0, 1
-L2_HINT, L2_HINT_LAST, L2_LOAD = 0, 1, 2
+L2_HINT, L2_HINT_LAST, L2_LOAD, L2_BULK = 0, 1, 2, 3
 OPT_PDL, OPT_SPLIT, OPT_GENERIC, OPT_CTAS_PER_SM, OPT_TENSOR, OPT_PROLOGUE, OPT_MAX_TILE = 0, 1, 2, 3, 4, 5, 6
 E_DRIVER, E_NO_CONTEXT, E_INVALID = -1000, -1001, -1002
 E_SHAPE, E_ALIGN, E_UNSUPPORTED, E_DEVICE, E_SCRATCH = -2001, -2002, -2003, -2004, -2005

@@ -2,7 +2,7 @@
 // (research/l2-prefetch/src/prefetch_kernels.cu:3-25):
 //   (const char* p, long long bytes, int stride, unsigned* sink)
 // Grid-stride over [p, p + bytes), one request per `stride` bytes; none of them
-// writes the range. Built into libklab_b200.so (klab_l2_prefetch) and, unchanged,
+// writes the range. l2_bulk is this library's own B200 kind (bulk-copy prefetch). Built into libklab_b200.so (klab_l2_prefetch) and, unchanged,
 // into a standalone cubin that the lab_* driver ABI loads by name.
 #include "common.cuh"
 #include "klab_kernels.h"
@@ -36,6 +36,25 @@ extern "C" __global__ void l2_load(const char* p, long long bytes, int stride, u
   if (bytes < 0 && acc == 0x9e3779b9u) sink[0] = acc;
 }
 
+// B200 form: the copy engine fills L2. Each thread issues cp.async.bulk.prefetch.L2 requests of
+// `stride` bytes (clamped to [16, 64 KiB], a multiple of 16) over the 16-byte-aligned interior of
+// [p, p + bytes); a handful of threads cover tens of MB with a few hundred instructions. The
+// unaligned head and tail (under 16 bytes each) are left out: a prefetch is only a hint.
+extern "C" __global__ void l2_bulk(const char* p, long long bytes, int stride, unsigned* sink) {
+  if (bytes <= 0) return;
+  const unsigned long long a = reinterpret_cast<unsigned long long>(p);
+  const unsigned long long lo = (a + 15ull) & ~15ull, hi = (a + static_cast<unsigned long long>(bytes)) & ~15ull;
+  if (hi <= lo) return;
+  const long long span = static_cast<long long>(hi - lo);
+  const long long chunk = static_cast<long long>(min(max(stride, 16), 65536) & ~15);
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x * chunk;
+  for (long long off = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) * chunk; off < span;
+       off += step) {
+    const unsigned n = static_cast<unsigned>(min(chunk, span - off));
+    klab::bulk_prefetch_l2(reinterpret_cast<const void*>(lo + off), n);
+  }
+}
+
 namespace klab {
 cudaError_t launch_l2_prefetch(const void* p, long long bytes, int blocks, int stride, int threads, int kind,
                                unsigned* sink, cudaStream_t stream) {
@@ -44,6 +63,8 @@ cudaError_t launch_l2_prefetch(const void* p, long long bytes, int blocks, int s
     l2_hint<<<blocks, threads, 0, stream>>>(c, bytes, stride, sink);
   else if (kind == KLAB_L2_HINT_LAST)
     l2_hint_last<<<blocks, threads, 0, stream>>>(c, bytes, stride, sink);
+  else if (kind == KLAB_L2_BULK)
+    l2_bulk<<<blocks, threads, 0, stream>>>(c, bytes, stride, sink);
   else
     l2_load<<<blocks, threads, 0, stream>>>(c, bytes, stride, sink);
   return cudaGetLastError();

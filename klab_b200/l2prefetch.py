@@ -16,8 +16,9 @@ import torch
 
 from . import _native
 
-KERNELS = ("l2_hint", "l2_load", "l2_hint_last")
-_KIND = {"l2_hint": _native.L2_HINT, "l2_hint_last": _native.L2_HINT_LAST, "l2_load": _native.L2_LOAD}
+KERNELS = ("l2_hint", "l2_load", "l2_hint_last", "l2_bulk")
+_KIND = {"l2_hint": _native.L2_HINT, "l2_hint_last": _native.L2_HINT_LAST, "l2_load": _native.L2_LOAD,
+         "l2_bulk": _native.L2_BULK}
 _modules = {}
 _sink = {}
 
@@ -33,7 +34,9 @@ def module(device=None):
 
 
 def prefetch(tensor, blocks, kernel="l2_hint", stride=128, threads=256, nbytes=None):
-    """Enqueue an L2 prefetch of `tensor`'s bytes (or its first `nbytes`) on the current stream."""
+    """Enqueue an L2 prefetch of `tensor`'s bytes (or its first `nbytes`) on the current stream.
+    kernel "l2_bulk" (this library's own) hands `stride` bytes per request (16 B .. 64 KiB) to the
+    bulk-copy engine, so a few threads cover the range."""
     if blocks <= 0:
         return
     if kernel not in _KIND:

@@ -24,7 +24,7 @@ def test_tune_candidates_never_change_outputs():
     x0 = torch.randn(1, dim, device="cuda").to(torch.bfloat16)
     plan, report = at.tune(ops, reads, x0, at.stage_bytes(reads[0]), rounds=3)
     assert report["best"] in at.candidates(at.stage_bytes(reads[0]))
-    assert plan is None or plan["kernel"] == "l2_hint"
+    assert plan is None or plan["kernel"] in ("l2_hint", "l2_bulk")
     plans, history = at.tune_positions(ops, reads, x0, period=2, rounds=3, log=None)
     assert len(plans) == 2 and len(history) == 2
 

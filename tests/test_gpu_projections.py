@@ -396,13 +396,18 @@ def test_prefetch_never_writes_and_driver_abi_path():
 
     t = torch.randn(1 << 20, device="cuda")
     before = t.clone()
-    for kernel in ("l2_hint", "l2_hint_last", "l2_load"):
+    for kernel in ("l2_hint", "l2_hint_last", "l2_load", "l2_bulk"):
         l2prefetch.prefetch(t, blocks=4, kernel=kernel, stride=32)
         l2prefetch.prefetch(t, blocks=2, kernel=kernel, nbytes=4096)
+    # bulk requests: clamped request sizes, an unaligned start and a length under 16 bytes
+    b = t.view(torch.uint8)
+    for stride, lo, n in ((1 << 20, 0, b.numel()), (17, 3, 100_001), (65536, 5, 9), (16, 0, 0)):
+        l2prefetch.prefetch(b[lo:lo + n] if n else b[:1], blocks=3, kernel="l2_bulk", stride=stride, threads=32,
+                            nbytes=n)
     import ctypes as ct
     mod = l2prefetch.module()
     sink = torch.zeros(1, dtype=torch.int32, device="cuda")
-    for kernel in ("l2_hint", "l2_hint_last", "l2_load"):
+    for kernel in ("l2_hint", "l2_hint_last", "l2_load", "l2_bulk"):
         mod.launch(kernel, (8, 1), 256, t, ct.c_longlong(t.numel() * 4), ct.c_int(128), sink)
     torch.cuda.synchronize()
     assert torch.equal(t, before)
