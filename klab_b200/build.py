@@ -26,6 +26,7 @@ OBJ = OUT / "obj"
 LIBRARY = OUT / "libklab_b200.so"
 ALIAS = OUT / "libkernel_lab.so"  # the reference's library name (native/build/libkernel_lab.so)
 PREFETCH_CUBIN = OUT / "prefetch_kernels.cubin"
+LAUNCHER = HERE.parent / "bin" / "klab"   # the reference's bin/klab (native/cli.cpp)
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler",
@@ -105,7 +106,23 @@ def build(clean: bool = False, verbose: bool = False, out_dir: Path | None = Non
     if ALIAS.is_symlink() or ALIAS.exists():
         ALIAS.unlink()
     ALIAS.symlink_to(LIBRARY.name)
+    if out_dir is None:
+        build_launcher()
     return LIBRARY
+
+
+def build_launcher() -> Path:
+    """bin/klab from csrc/cli.cpp (g++, no CUDA): execs `python -m klab_b200.cli`."""
+    source = CSRC / "cli.cpp"
+    if _stale(LAUNCHER, [source]):
+        LAUNCHER.parent.mkdir(exist_ok=True)
+        cxx = shutil.which(os.environ.get("CXX", "g++")) or "g++"
+        tmp = LAUNCHER.with_suffix(".new")
+        _run([cxx, "-O2", "-std=c++17", "-Wall", "-Wextra", "-Werror",
+              f'-DKLAB_PROJECT_ROOT="{HERE.parent}"', f'-DKLAB_PYTHON="{sys.executable}"', str(source), "-o",
+              str(tmp)])
+        tmp.replace(LAUNCHER)
+    return LAUNCHER
 
 
 def main(argv=None):
