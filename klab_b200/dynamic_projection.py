@@ -9,7 +9,9 @@ prepare_projection(w, tokens, profile, output_dtype):
   the half projection); with a held-out report (a dict or a JSON path in the
   reference's format), projection_policy.choose picks the route: lossless_* and
   fp28_* pack the weights losslessly, the other custom configurations use the
-  plain plan, vendor configurations call torch.mm. The reference additionally
+  plain plan, vendor configurations run through vendor_call (the operator
+  kernel_lab::dynamic_vendor). kernel_lab::dynamic_tiny exposes the fixed-K FP32
+  projection as an operator. The reference additionally
   checks its report against the hashes of its own source files and the GPU's
   UUID; those describe its validation runs and are not carried over.
 """
@@ -24,10 +26,36 @@ import torch
 from . import _native
 from . import lossless_weights
 from . import packed_fp32
+from .kernel_lab import default_lab
 from .prepared import PreparedPlan
 from .projection_policy import choose
+from .vendor import vendor_call
 
 _WFMT = {torch.float32: _native.W_F32, torch.float16: _native.W_F16, torch.bfloat16: _native.W_BF16}
+
+
+@torch.library.custom_op("kernel_lab::dynamic_vendor", mutates_args=(), device_types="cuda")
+def dynamic_vendor(x: torch.Tensor, w: torch.Tensor, config: str) -> torch.Tensor:
+    """x . W^T (FP32) through the vendor route `config` (dynamic_projection.py:47-55)."""
+    return vendor_call(x, w, config)
+
+
+@dynamic_vendor.register_fake
+def _dynamic_vendor_fake(x, w, config):
+    return x.new_empty((x.shape[0], w.shape[1] if "packed" in config else w.shape[0]), dtype=torch.float32)
+
+
+@torch.library.custom_op("kernel_lab::dynamic_tiny", mutates_args=(), device_types="cuda")
+def dynamic_tiny(x: torch.Tensor, w: torch.Tensor, threads: int, vector: int) -> torch.Tensor:
+    """KernelLab.tiny_matmul as an operator (dynamic_projection.py:58-63): FP32 x . W^T for
+    K in {64, ..., 1024}; threads / vector are validated launch hints."""
+    with torch.cuda.device(x.device):
+        return default_lab().tiny_matmul(x, w, threads, vector)
+
+
+@dynamic_tiny.register_fake
+def _dynamic_tiny_fake(x, w, threads, vector):
+    return x.new_empty((x.shape[0], w.shape[0]))
 
 
 def _load_profile(profile):
@@ -62,7 +90,8 @@ class PreparedProjection:
         self.packed, self.w, self.native = None, w, None
         if self.plan["backend"] == "vendor":
             self.w = w.T.contiguous() if "packed" in self.strategy else w
-            torch.mm(torch.zeros(tokens, self.k, device=w.device, dtype=w.dtype), w.T)
+            # vendor handles and workspaces exist before any later graph capture
+            vendor_call(torch.zeros(tokens, self.k, device=w.device, dtype=w.dtype), self.w, self._vendor_config())
             return
         if self.strategy.startswith("lossless_") and w.dtype == torch.float32:
             self.packed = lossless_weights.pack_weights(w)
@@ -78,14 +107,20 @@ class PreparedProjection:
         if x.ndim != 2 or tuple(x.shape) != (self.m, self.k):
             raise ValueError("Input shape differs; prepare a plan for this token count")
         if self.plan["backend"] == "vendor":
-            w_t = self.w if "packed" in self.strategy else self.w.T
-            return torch.mm(x, w_t, out_dtype=torch.float32, out=out) if x.dtype != torch.float32 \
-                else torch.mm(x, w_t, out=out)
+            config = self._vendor_config()
+            return vendor_call(x, self.w, config, out) if out is not None else dynamic_vendor(x, self.w, config)
         if isinstance(self.packed, lossless_weights.LosslessWeights):
             return lossless_weights.fused_linear(x, self.packed, out=out)
         if isinstance(self.packed, packed_fp32.PackedFP32Weights):
             return packed_fp32.fused_linear(x, self.packed, out=out)
         return self.native.launch(x, self.w, out=out)
+
+    def _vendor_config(self):
+        """The report's vendor route when it names one of vendor_call's, else torch.mm."""
+        from .vendor import CONFIGS
+
+        return self.strategy if self.strategy in CONFIGS else ("torch_mm" if self.dtype == torch.float32
+                                                                else "torch_mm_out_fp32")
 
     __call__ = linear
 
