@@ -38,7 +38,6 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 METRIC = "achieved HBM GB/s vs 8 TB/s & µs/projection at M=1..16; chain tok/s 1/2/4/8 GPU"
-L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 
 
@@ -135,39 +134,7 @@ def barrier(world):
         dist.barrier()
 
 
-def graph_of(torch, fn, stream):
-    stream.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(stream):
-        fn()
-    torch.cuda.current_stream().wait_stream(stream)
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        fn()
-    return graph
-
-
-def time_graph(torch, graph, calls, rounds):
-    """Median µs per call over `rounds` replays of a graph of `calls` calls."""
-    times = []
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    for _ in range(rounds):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        graph.replay()
-        b.record()
-        b.synchronize()
-        times.append(a.elapsed_time(b) * 1000.0 / calls)
-    return statistics.median(times)
-
-
 # ---------------------------------------------------------------- per-config projections (N=1)
-
-def ring_count(nbytes):
-    return max(8, math.ceil(max(2 << 30, 16 * L2_BYTES) / nbytes))
-
 
 def bench_projections(torch, peak, quick=False):
     """Configs 1-4 through the public API over cold-L2 weight rings, with cuBLAS
@@ -175,7 +142,7 @@ def bench_projections(torch, peak, quick=False):
     import torch.nn.functional as F
 
     from klab_b200 import compressed_bf16 as cb
-    from klab_b200 import fp4, int8_weights
+    from klab_b200 import fp4, int8_weights, measure
 
     dev = torch.device("cuda")
     stream = torch.cuda.Stream()
@@ -184,14 +151,14 @@ def bench_projections(torch, peak, quick=False):
     rounds = 5 if quick else 15
 
     def record(name, m, n, k, nbytes, fn_ours, fn_vendor, ring):
-        g = graph_of(torch, lambda: [fn_ours(i) for i in range(ring)], stream)
-        us = time_graph(torch, g, ring, rounds)
+        g = measure.graph_of(lambda: [fn_ours(i) for i in range(ring)], stream)
+        us = measure.time_graph(g, ring, rounds)
         del g
         row = {"config": name, "m": m, "n": n, "k": k, "bytes": nbytes, "us": round(us, 3),
                "gbs": round(nbytes / us / 1e3, 1), "frac_of_measured_peak": round(nbytes / us / 1e3 / peak, 4)}
         if fn_vendor is not None:
-            gv = graph_of(torch, lambda: [fn_vendor(i) for i in range(ring)], stream)
-            vus = time_graph(torch, gv, ring, rounds)
+            gv = measure.graph_of(lambda: [fn_vendor(i) for i in range(ring)], stream)
+            vus = measure.time_graph(gv, ring, rounds)
             del gv
             row["cublas_us"] = round(vus, 3)
             row["speedup_vs_cublas"] = round(vus / us, 3)
@@ -206,7 +173,7 @@ def bench_projections(torch, peak, quick=False):
     n = k = 4096
     w = bf16_normal((n, k), 0.02, 1)
     nbytes = n * k * 2 + k * 2 + n * 2
-    ring = ring_count(n * k * 2)
+    ring = measure.ring_count(n * k * 2)
     ws = [w.clone() for _ in range(ring)]
     x = bf16_normal((1, k), 0.02, 2)
     outs = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
@@ -222,7 +189,7 @@ def bench_projections(torch, peak, quick=False):
     q = int8_weights.quantize_weights_per_row(w32)
     deq = q.dequantize().to(torch.bfloat16)
     del w32
-    ring = ring_count(n * k)
+    ring = measure.ring_count(n * k)
     codes = [q.codes.clone() for _ in range(ring)]
     vring = max(4, math.ceil(ring / 2))
     deqs = [deq.clone() for _ in range(vring)]
@@ -242,7 +209,7 @@ def bench_projections(torch, peak, quick=False):
     q = fp4.quantize_weights_f16(w32)
     deq = q.dequantize().to(torch.bfloat16)
     del w32
-    ring = ring_count(n * k // 2 + n * k // 16)
+    ring = measure.ring_count(n * k // 2 + n * k // 16)
     packs = [(q.packed.clone(), q.scales.clone()) for _ in range(ring)]
     vring = max(4, math.ceil(ring / 4))
     deqs = [deq.clone() for _ in range(vring)]
@@ -263,11 +230,11 @@ def bench_projections(torch, peak, quick=False):
         bits = w.view(torch.int16).cpu().numpy().view("uint16")
         layers.append((cb.upload(cb.pack_bits(bits), dev), w))
     per = layers[0][0].storage_bytes
-    ring = ring_count(per)
+    ring = measure.ring_count(per)
     coded = [layers[i % 8][0] for i in range(8)]
     coded += [cb.PackedBF16(coded[i % 8].payload.clone(), coded[i % 8].metadata.clone(), n, k,
                             coded[i % 8].source_sha256, 1, coded[i % 8].module) for i in range(8, ring)]
-    raws = [layers[i % 8][1] for i in range(8)] + [layers[i % 8][1].clone() for i in range(8, ring_count(n * k * 2))]
+    raws = [layers[i % 8][1] for i in range(8)] + [layers[i % 8][1].clone() for i in range(8, measure.ring_count(n * k * 2))]
     x = bf16_normal((1, k), 1.0, 9)
     out = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
     storage = sum(c.storage_bytes for c in coded) / len(coded)
@@ -288,13 +255,14 @@ def bench_decode_attention(torch, peak, quick=False):
     caches. bytes = the K and V rows read (L + 1 per kv head) + q, the new rows and the output."""
     import torch.nn.functional as F
 
+    from klab_b200 import measure
     from klab_b200.decode_attn import decode_attention
 
     dev = torch.device("cuda")
     stream = torch.cuda.Stream()
     heads, kv, cap = 32, 8, 4096
     per = 2 * kv * cap * 64 * 2
-    ring = max(8, math.ceil(4 * L2_BYTES / per))
+    ring = max(8, math.ceil(4 * measure.L2_BYTES / per))
     gen = torch.Generator(device=dev).manual_seed(21)
     caches = [(torch.randn((kv, cap, 64), generator=gen, device=dev).to(torch.bfloat16),
                torch.randn((kv, cap, 64), generator=gen, device=dev).to(torch.bfloat16)) for _ in range(ring)]
@@ -312,11 +280,11 @@ def bench_decode_attention(torch, peak, quick=False):
                                            caches[i][1][:, :length + 1].unsqueeze(0), enable_gqa=True)
 
         nbytes = 2 * kv * (length + 1) * 64 * 2 + heads * 64 * 2 * 2 + 2 * kv * 64 * 2
-        g = graph_of(torch, lambda: [ours(i) for i in range(ring)], stream)
-        us = time_graph(torch, g, ring, 5 if quick else 15)
+        g = measure.graph_of(lambda: [ours(i) for i in range(ring)], stream)
+        us = measure.time_graph(g, ring, 5 if quick else 15)
         del g
-        gv = graph_of(torch, lambda: [sdpa(i) for i in range(ring)], stream)
-        vus = time_graph(torch, gv, ring, 5 if quick else 15)
+        gv = measure.graph_of(lambda: [sdpa(i) for i in range(ring)], stream)
+        vus = measure.time_graph(gv, ring, 5 if quick else 15)
         del gv
         rows.append({"heads": heads, "kv_heads": kv, "length": length, "capacity": cap, "bytes": nbytes,
                      "us": round(us, 3), "gbs": round(nbytes / us / 1e3, 1),
@@ -325,6 +293,39 @@ def bench_decode_attention(torch, peak, quick=False):
     del caches
     torch.cuda.empty_cache()
     return rows
+
+
+def bench_prefetch(torch, quick=False):
+    """Does a side-stream L2 prefetch lift a C5-shaped pair of projections on B200? The
+    autotuner's per-position search (prefetch_autotune.tune_positions: every candidate of
+    both kinds, successive halving, bootstrap lower bound > +1 %, bit-identical outputs)
+    over 8 layers of (o 4096x4096, gate 14336x4096) BF16 projections at M=1 with distinct
+    weights (1.2 GB, cold L2), timed by CUDA events on graph replays."""
+    from klab_b200 import compressed_bf16 as cb
+    from klab_b200 import prefetch_autotune as at
+
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    shapes = [(4096, 4096), (14336, 4096)] * 8
+    weights = [torch.randn(s, generator=gen, device="cuda").mul_(0.02).to(torch.bfloat16) for s in shapes]
+    outs = [torch.empty((1, s[0]), device="cuda", dtype=torch.bfloat16) for s in shapes]
+    x0 = torch.randn((1, 4096), generator=gen, device="cuda").to(torch.bfloat16)
+
+    def op(i):
+        # every op reads the same token x0 (the pair's weights, not its data flow, set the traffic)
+        return lambda y, i=i: (cb.raw_linear(x0, weights[i], threads=128, vector=8, output_dtype="bf16",
+                                             out=outs[i]), y)[1]
+
+    ops = [op(i) for i in range(len(shapes))]
+    reads = [[w] for w in weights]
+    plans, history = at.tune_positions(ops, reads, x0, period=2, rounds=3 if quick else 7, log=None)
+    rows = [{"position": ("o" if h["pos"] == 0 else "gate" if h["pos"] == 1 else "both"), "best": h["best"],
+             "saved_pct": round(h["saved_vs_current"], 3), "ci95": [round(v, 3) for v in h["ci95"]],
+             "kept": h["kept"]} for h in history]
+    del weights, outs
+    torch.cuda.empty_cache()
+    return {"workload": "8 x (o 4096x4096, gate 14336x4096) bf16 M=1, distinct weights (1.2 GB)",
+            "plans": [p if p is None else {k: p[k] for k in ("kernel", "blocks", "nbytes")} for p in plans],
+            "search": rows}
 
 
 # ---------------------------------------------------------------- dominant kernel roofline
@@ -338,7 +339,7 @@ def bench_dominant_kernel(torch, chain, peak, rounds=10):
     """Average duration of the chain's gate projection (the largest BF16 GEMV),
     timed with CUDA events on its launch stream over the chain's 32 distinct gate
     weights (cold L2), inside a CUDA graph."""
-    from klab_b200 import _native
+    from klab_b200 import _native, measure
 
     shape = chain.shape
     gates = [layer["gate"] for layer in chain.layers]
@@ -352,9 +353,9 @@ def bench_dominant_kernel(torch, chain, peak, rounds=10):
             _native.gemv(_native.W_BF16, _native.DT_BF16, h, w, None, None, out[:, rows[0]:], _native.DT_BF16,
                          h.shape[0], n_shard, shape.hidden, ldo=n)
 
-    g = graph_of(torch, run, stream)
+    g = measure.graph_of(run, stream)
     torch.cuda.nvtx.range_push("dominant")   # ncu --nvtx-include "dominant/" selects these launches
-    us = time_graph(torch, g, len(gates), rounds)
+    us = measure.time_graph(g, len(gates), rounds)
     torch.cuda.nvtx.range_pop()
     del g
     nbytes = n_shard * shape.hidden * 2 + shape.hidden * 2 + n_shard * 2
@@ -362,63 +363,155 @@ def bench_dominant_kernel(torch, chain, peak, rounds=10):
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
             "frac": round(achieved / peak, 4),
             "traffic": NCU_GATE_TRAFFIC_BYTES if chain.world == 1 else None,
-            "traffic_unit": "bytes per launch (ncu capture, profiles/stream_gemv_gate_bf16_m1.md)",
+            "traffic_unit": "bytes per launch, from one ncu capture of this launch at N=1 "
+                            "(profiles/stream_gemv_gate_bf16_m1.md); a cross-check, not measured in this run",
             "kernel": "stream_gemv_kernel<W_BF16,X_BF16,SMEM16,1>",
             "launch": f"gate {n_shard}x{shape.hidden} bf16, M=1", "bytes_per_launch": nbytes,
             "us_per_launch": round(us, 3)}
 
 
-# ---------------------------------------------------------------- CPU baseline (oracle port)
+# ---------------------------------------------------------------- CPU baselines
+
+LAYER_SHAPES = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096),
+                (4096, 14336)]   # q, k, v, o, gate, up, down (one decoder layer of the chain)
+
+
+def host_threads():
+    """All host cores, whatever OMP_NUM_THREADS a launcher set (torchrun sets 1)."""
+    return os.cpu_count() or 1
+
+
+def cpu_reference_tok_s(seconds=10.0):
+    """The reference's CPU path for this workload: torch.nn.functional.linear on CPU BF16
+    tensors (the "bf16_reference / torch F.linear path" of benchmark config 1; torch 2.11 as
+    the reference's requirements.lock pins it), with torch.set_num_threads(all host cores),
+    over one 7-projection decoder layer of the chain (up feeds down), repeated for about
+    `seconds` and scaled to 32 layers per token."""
+    import torch
+
+    before = torch.get_num_threads()
+    torch.set_num_threads(host_threads())
+    try:
+        gen = torch.Generator().manual_seed(0)
+        weights = [(torch.randn(shape, generator=gen) * 0.02).to(torch.bfloat16) for shape in LAYER_SHAPES]
+        h = torch.randn((1, 4096), generator=gen).to(torch.bfloat16)
+        F = torch.nn.functional
+
+        def layer():
+            for w in weights[:6]:
+                y = F.linear(h, w)
+            return F.linear(y, weights[6])          # y is up (the sixth projection): it feeds down
+
+        layer()                                     # warm-up
+        layers, t0 = 0, time.perf_counter()
+        while True:
+            layer()
+            layers += 1
+            if time.perf_counter() - t0 >= seconds:
+                break
+        elapsed = time.perf_counter() - t0
+        threads = torch.get_num_threads()
+    finally:
+        torch.set_num_threads(before)
+    per_token = elapsed / layers * 32
+    return {"value": round(1.0 / per_token, 4), "unit": "tok/s", "cores": int(threads), "kind": "reference",
+            "sample": f"{layers} passes over one 7-projection decoder layer (torch {torch.__version__} F.linear, "
+                      f"CPU bf16, {threads} threads), {elapsed:.1f} s, scaled x32 layers per token"}
+
 
 def cpu_oracle_tok_s(seconds=10.0):
-    """The CPU oracle's FP64 projection (oracle.gemv.projection64 + round_bf16_bits)
-    timed on one decoder layer of the chain (7 projections), scaled to tokens/s
-    for 32 layers. Weights are pre-widened to FP64 outside the timed region."""
+    """The FP64 oracle port (oracle.gemv.projection64 + round_bf16_bits) timed the same way
+    on all host cores; weights are widened to FP64 outside the timed region."""
     import numpy as np
 
     from oracle import bf16 as ob
     from oracle import gemv as og
 
     try:
-        from threadpoolctl import threadpool_info
-        cores = max([p.get("num_threads", 1) for p in threadpool_info()] or [os.cpu_count() or 1])
+        from threadpoolctl import threadpool_limits
+        limits = threadpool_limits(host_threads())
     except Exception:
-        cores = os.cpu_count() or 1
-    shapes = [(4096, 4096), (1024, 4096), (1024, 4096), (4096, 4096), (14336, 4096), (14336, 4096), (4096, 14336)]
-    rng = np.random.default_rng(0)
-    weights = [ob.bf16_values(og.normal_bf16_bits(i, shape, 0.02)) for i, shape in enumerate(shapes)]
-    x = ob.bf16_values(og.normal_bf16_bits(99, (1, 4096), 1.0))
-    up = ob.bf16_values(og.normal_bf16_bits(98, (1, 14336), 1.0))
+        limits = None
+    import torch
+
+    gen = torch.Generator().manual_seed(0)
+
+    def values(shape, std):
+        t = (torch.randn(shape, generator=gen) * std).to(torch.bfloat16)
+        return ob.bf16_values(t.view(torch.int16).numpy().view(np.uint16))
+
+    weights = [values(shape, 0.02) for shape in LAYER_SHAPES]
+    x, up = values((1, 4096), 1.0), values((1, 14336), 1.0)
     layers = 0
     t0 = time.perf_counter()
     while True:
         for i, w in enumerate(weights):
-            src = up if i == 6 else x
-            ob.round_bf16_bits(og.projection64(src, w))
+            ob.round_bf16_bits(og.projection64(up if i == 6 else x, w))
         layers += 1
         if time.perf_counter() - t0 >= seconds:
             break
     elapsed = time.perf_counter() - t0
-    del rng
-    per_token = elapsed / layers * 32
-    return {"value": round(1.0 / per_token, 4), "unit": "tok/s", "cores": int(cores), "kind": "port",
-            "sample": f"{layers} passes over one 7-projection decoder layer (FP64 oracle, 218M weights), "
-                      f"{elapsed:.1f} s, scaled x32 layers per token"}
+    if limits is not None:
+        limits.restore_original_limits()
+    return {"value": round(layers / (32.0 * elapsed), 4), "unit": "tok/s", "cores": host_threads(), "kind": "port",
+            "sample": f"{layers} passes over one 7-projection decoder layer (FP64 oracle), {elapsed:.1f} s, "
+                      f"scaled x32 layers per token"}
+
+
+def chain_parity(torch):
+    """The checker in the CPU leg: the benchmark chain's first two layers (same seeds as the
+    timed chain) on this GPU against the FP64 oracle with the chain's per-stage BF16
+    rounding (every projection output within the reference's check_outputs interval and one
+    BF16 ulp of FP64; down checked from the GPU's own up output)."""
+    import numpy as np
+
+    from klab_b200.chain import ChainShape, ProjectionChain
+    from oracle import bf16 as ob
+    from oracle import gemv as og
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+    gen = torch.Generator(device="cuda").manual_seed(1234)
+    x = torch.randn((1, 4096), generator=gen, device="cuda").to(torch.bfloat16)
+    worst, passed, checked = 0, True, 0
+    h_bits = bits(x)
+    for layers in (1, 2):
+        chain = ProjectionChain(ChainShape(layers=layers), seed=0)
+        h = chain.forward_eager(x)
+        entry = chain.layers[layers - 1]
+        got = dict(chain.a_out, up=chain.up_full, down=h)
+        for name in ("q", "k", "v", "o", "gate", "up", "down"):
+            src = bits(chain.up_full) if name == "down" else h_bits
+            rep = ob.check_outputs(og.bf16_projection64(src, bits(entry[name][0])), got[name].float().cpu().numpy(),
+                                   output_dtype="bf16")
+            passed &= bool(rep["passed"]) and rep["max_ulp_error"] <= 1
+            worst = max(worst, int(rep["max_ulp_error"]))
+            checked += int(rep["elements_checked"])
+        h_bits = bits(h)
+        del chain, h, got
+        torch.cuda.empty_cache()
+    return {"layers_checked": 2, "elements_checked": checked, "passed": passed, "max_ulp_error": worst,
+            "against": "FP64 oracle, check_outputs interval + <= 1 bf16 ulp"}
 
 
 # ---------------------------------------------------------------- reference arm
 
 def run_reference(args, rank, world):
+    """The reference's CPU implementation of the path (torch F.linear on CPU BF16, all host
+    cores) on rank 0; other ranks exit without work."""
     if rank != 0:
         return 0
     seconds = max(3.0, min(30.0, 2.0 * (args.steps + args.warmup) / 10.0))
-    base = cpu_oracle_tok_s(seconds)
+    base = cpu_reference_tok_s(seconds)
     line = {"metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(1000.0 / base["value"], 3), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": "c5_chain_llama3_8b_shapes_32_layers_m1", "layers": 32, "M": 1,
-                       "hidden": 4096, "ffn": 14336, "kv": 1024},
+                       "hidden": 4096, "ffn": 14336, "kv": 1024,
+                       "parallelism": f"column-shard x{world}" if world > 1 else "column-shard x1",
+                       "bytes_per_token": 13_958_643_712},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -528,17 +621,21 @@ def main(argv=None):
     roofline["peak_kind"] = peak_kind
     status = _native.device_status(clear=True)
 
-    projections = attention = None
+    projections = attention = prefetch = None
     if world == 1 and not args.no_projections:
         del chain
         torch.cuda.empty_cache()
         chain = None
         projections = bench_projections(torch, peak, quick=args.quick)
         attention = bench_decode_attention(torch, peak, quick=args.quick)
+        prefetch = bench_prefetch(torch, quick=args.quick)
 
-    cpu = None
+    cpu = parity = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_oracle_tok_s(10.0 if not args.quick else 3.0)
+        seconds = 10.0 if not args.quick else 3.0
+        cpu = cpu_reference_tok_s(seconds)
+        cpu["oracle_fp64"] = cpu_oracle_tok_s(seconds)
+        parity = chain_parity(torch)
 
     if rank == 0:
         value = args.steps / step_s
@@ -566,10 +663,14 @@ def main(argv=None):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if parity is not None:
+            line["parity"] = parity
         if projections is not None:
             line["projections"] = projections
         if attention is not None:
             line["decode_attention"] = attention
+        if prefetch is not None:
+            line["l2_prefetch"] = prefetch
         print(json.dumps(line), flush=True)
 
     if chain is not None:

@@ -13,12 +13,15 @@
 // array's name is only a host-side stand-in for the symbol, so its device
 // address is obtained once per device with cudaGetSymbolAddress (with that
 // device current) and cached. That set-up happens on the first call on each
-// device: make that first call before any CUDA graph capture.
+// device: make that first call before any CUDA graph capture. The cached address
+// belongs to the device's primary context: after cudaDeviceReset on a device, its
+// cached address is stale, so use this entry point only in processes that do not
+// reset their devices.
 //
 // All calls share the array and it keeps the last call's contents. The first
 // 64 KiB hold the split-K completion tickets, which must start at zero: every
-// call clears the tickets it can use with cudaMemsetAsync on its stream before
-// the launch (a memset, not an allocation). Calls whose kernels can overlap on
+// call that splits clears that whole 64 KiB region with cudaMemsetAsync on its
+// stream before the launch (a memset, not an allocation). Calls whose kernels can overlap on
 // the GPU (different streams, or different host threads) race on the array and
 // must be serialized by the caller. Shapes whose split-K scratch exceeds the
 // array are rejected with KLAB_E_SCRATCH before any device work.

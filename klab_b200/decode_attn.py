@@ -35,9 +35,11 @@ def module():
     return get_module()
 
 
-def _workspace(device, heads, kv_heads, max_len):
-    """Scratch for heads * ceil(max_len / 64) split records (enough for any length) and the tickets."""
-    key = (device, heads, kv_heads, max_len)
+def _workspace(device, stream, heads, kv_heads, max_len):
+    """Scratch for heads * ceil(max_len / 64) split records (enough for any length) and the
+    tickets, one set per (device, stream, shape): calls on different streams may overlap on
+    the GPU, so they never share tickets or records. Calls on one stream run in order."""
+    key = (device, stream.cuda_stream, heads, kv_heads, max_len)
     if key not in _work:
         _work[key] = (torch.empty(heads * -(-max_len // CHUNK) * (HD + 2), device=device, dtype=torch.float32),
                       torch.zeros(kv_heads, device=device, dtype=torch.int32))
@@ -48,8 +50,8 @@ def _launch(q, k_new, v_new, k_cache, v_cache, out, len_ptr, length):
     kv_heads, max_len, _ = k_cache.shape
     heads = q.numel() // HD
     get_module(q.device)
-    scratch, tickets = _workspace(q.device, heads, kv_heads, max_len)
     stream = torch.cuda.current_stream(q.device)
+    scratch, tickets = _workspace(q.device, stream, heads, kv_heads, max_len)
     with torch.cuda.device(q.device):
         rc = _native.lib().klab_decode_attention(q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), k_cache.data_ptr(),
                                                  v_cache.data_ptr(), out.data_ptr(), scratch.data_ptr(),
