@@ -69,3 +69,29 @@ def test_klab_run_and_check_end_to_end(tmp_path):
     assert r.returncode == 0, (r.stdout, r.stderr)
     summary = json.loads(r.stdout)
     assert summary["status"] == "passed" and summary["passed"] >= 2 and summary["failed"] == 0
+
+
+@pytest.mark.parametrize("m,n,k,out", [(1, 4096, 4096, torch.bfloat16), (4, 1024, 2048, torch.float32)])
+def test_frozen_cublaslt_plan_round_trip(m, n, k, out):
+    """tune -> freeze -> restore: the restored plan runs the same algorithm (same bits) and
+    both meet the FP64 oracle; a record restored with another shape is refused."""
+    import json
+
+    from klab_b200 import lt_baseline as lt
+
+    x = torch.from_numpy(og.normal_f32(1, (m, k))).to(torch.bfloat16).cuda()
+    w = torch.from_numpy(og.normal_f32(2, (n, k), 0.02)).to(torch.bfloat16).cuda()
+    plan = lt.tune_plan(x, w, out, rounds=3)
+    y = torch.empty(m, n, device="cuda", dtype=out)
+    plan.run(x, w, y)
+    record = json.loads(json.dumps(plan.freeze()))
+    again = lt.LtPlan.restore(record, x.device)
+    y2 = torch.empty_like(y)
+    again.run(x, w, y2)
+    torch.cuda.synchronize()
+    assert torch.equal(y.view(torch.uint8), y2.view(torch.uint8))
+    ref = og.projection64(x.double().cpu().numpy(), w.double().cpu().numpy())
+    report = ob.check_outputs(ref, y.float().cpu().numpy(), output_dtype="bf16" if out == torch.bfloat16 else "fp32")
+    assert report["passed"], report
+    with pytest.raises(ValueError):
+        lt.validate_frozen(record, lt.runtime_context(x.device, x.dtype, out, m + 1, n, k))
