@@ -452,6 +452,19 @@ class ProjectionChain:
         self.graph.replay()
         return self.out
 
+    def step_guarded(self, guard, x=None):
+        """One token step with host-side failure detection (liveness.StepGuard): every rank
+        agrees, bounded, on the step's epoch before launching; after the step the device status
+        word is checked. Replays the captured graph, or runs eagerly on x when nothing is
+        captured. Raises a liveness.PeerFailure subclass or liveness.DeviceWaitExpired."""
+        self._guard_epoch = getattr(self, "_guard_epoch", 0) + 1
+        guard.enter(self._guard_epoch)
+        out = self.replay() if self.graph is not None else self.forward_eager(x)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+            guard.check_device()
+        return out
+
     def release(self):
         """Drop the graph (release graphs holding NCCL calls before destroying the
         group) and, in p2p mode, unmap the peers' buffers and free this rank's
