@@ -137,12 +137,15 @@ def barrier(world):
 # ---------------------------------------------------------------- per-config projections (N=1)
 
 def bench_projections(torch, peak, quick=False):
-    """Configs 1-4 through the public API over cold-L2 weight rings, with cuBLAS
-    (torch F.linear) on the same shapes (dequantized BF16 weights for INT8/FP4)."""
+    """Configs 1-4 through the public API over cold-L2 weight rings, beside two vendor
+    routes on the same shapes with BF16 weights (dequantized for INT8/FP4): torch F.linear
+    (cuBLAS) and a frozen cuBLASLt plan (the fastest heuristic candidate, lt_baseline).
+    The reference's own INT8 per-64 and E4M3/16 + global FP4 formats are timed too."""
     import torch.nn.functional as F
 
     from klab_b200 import compressed_bf16 as cb
     from klab_b200 import fp4, int8_weights, measure
+    from klab_b200 import lt_baseline as lt
 
     dev = torch.device("cuda")
     stream = torch.cuda.Stream()
@@ -150,18 +153,32 @@ def bench_projections(torch, peak, quick=False):
     results = []
     rounds = 5 if quick else 15
 
-    def record(name, m, n, k, nbytes, fn_ours, fn_vendor, ring):
+    def record(name, m, n, k, nbytes, fn_ours, ring, x=None, vw=None):
+        """vw: BF16 weights (a ring) for the vendor routes on x."""
         g = measure.graph_of(lambda: [fn_ours(i) for i in range(ring)], stream)
         us = measure.time_graph(g, ring, rounds)
         del g
         row = {"config": name, "m": m, "n": n, "k": k, "bytes": nbytes, "us": round(us, 3),
                "gbs": round(nbytes / us / 1e3, 1), "frac_of_measured_peak": round(nbytes / us / 1e3 / peak, 4)}
-        if fn_vendor is not None:
-            gv = measure.graph_of(lambda: [fn_vendor(i) for i in range(ring)], stream)
+        if vw is not None:
+            vr = len(vw)
+            gv = measure.graph_of(lambda: [F.linear(x, vw[i % vr]) for i in range(ring)], stream)
             vus = measure.time_graph(gv, ring, rounds)
             del gv
             row["cublas_us"] = round(vus, 3)
             row["speedup_vs_cublas"] = round(vus / us, 3)
+            try:
+                plan = lt.tune_plan(x, vw[0], torch.bfloat16, rounds=5)
+                lout = torch.empty((m, n), device=dev, dtype=torch.bfloat16)
+                gl = measure.graph_of(lambda: [plan.run(x, vw[i % vr], lout) for i in range(ring)], stream)
+                lus = measure.time_graph(gl, ring, rounds)
+                del gl
+                plan.close()
+                row["cublaslt_frozen_us"] = round(lus, 3)
+                row["speedup_vs_best_vendor"] = round(min(vus, lus) / us, 3)
+            except (lt.LtUnavailable, RuntimeError, ValueError) as error:
+                row["cublaslt_frozen_us"] = None
+                row["cublaslt_note"] = str(error)[:120]
         results.append(row)
         torch.cuda.empty_cache()
 
@@ -171,15 +188,15 @@ def bench_projections(torch, peak, quick=False):
 
     # C1: BF16 4096 x 4096, M = 1
     n = k = 4096
-    w = bf16_normal((n, k), 0.02, 1)
+    gen.manual_seed(0)   # benchmark config 1: W then x from one seed-0 stream, N(0, 0.02^2)
+    w = torch.randn((n, k), generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
+    x = torch.randn((1, k), generator=gen, device=dev).mul_(0.02).to(torch.bfloat16)
     nbytes = n * k * 2 + k * 2 + n * 2
     ring = measure.ring_count(n * k * 2)
     ws = [w.clone() for _ in range(ring)]
-    x = bf16_normal((1, k), 0.02, 2)
     outs = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
     record("c1_bf16_m1", 1, n, k, nbytes,
-           lambda i: cb.raw_linear(x, ws[i], threads=128, vector=8, output_dtype="bf16", out=outs),
-           lambda i: F.linear(x, ws[i]), ring)
+           lambda i: cb.raw_linear(x, ws[i], threads=128, vector=8, output_dtype="bf16", out=outs), ring, x, ws)
     del ws, w
 
     # C2: INT8 per-row, K=4096, N=14336, M in {1, 4, 16}
@@ -199,8 +216,19 @@ def bench_projections(torch, peak, quick=False):
         nbytes = n * k + n * 4 + m * k * 2 + m * n * 2
         record(f"c2_int8_row_m{m}", m, n, k, nbytes,
                lambda i: int8_weights.fused_linear(x, codes[i], q.scales, out=out, output_dtype=torch.bfloat16),
-               lambda i: F.linear(x, deqs[i % vring]), ring)
+               ring, x, deqs)
     del codes, deqs, deq, q
+    # the reference's INT8 format: FP32 scale per 64 columns (int8_weights.py:23-35), M = 1
+    gen.manual_seed(3)
+    q = int8_weights.quantize_weights(torch.randn((n, k), generator=gen, device=dev).mul_(0.02))
+    ring = measure.ring_count(n * k + n * k // 16)
+    codes = [(q.codes.clone(), q.scales.clone()) for _ in range(ring)]
+    x = bf16_normal((1, k), 1.0, 5)
+    out = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+    record("c2_int8_g64_m1 (reference format)", 1, n, k, n * k + n * k // 16 + k * 2 + n * 2,
+           lambda i: int8_weights.fused_linear(x, codes[i][0], codes[i][1], out=out, output_dtype=torch.bfloat16),
+           ring)
+    del codes, q
 
     # C3: FP4 E2M1 with FP16 scales per 32, K=N=8192, M in {1, 8}
     n = k = 8192
@@ -219,8 +247,19 @@ def bench_projections(torch, peak, quick=False):
         nbytes = n * k // 2 + n * k // 16 + m * k * 2 + m * n * 2
         record(f"c3_fp4_f16s32_m{m}", m, n, k, nbytes,
                lambda i: fp4.fused_linear(x, packs[i][0], packs[i][1], None, out=out, output_dtype=torch.bfloat16),
-               lambda i: F.linear(x, deqs[i % vring]), ring)
+               ring, x, deqs)
     del packs, deqs, deq, q
+    # the reference's FP4 format: E4M3 scale per 16 columns and an FP32 global scale (fp4.py:33-60), M = 1
+    gen.manual_seed(5)
+    q = fp4.quantize_weights(torch.randn((n, k), generator=gen, device=dev).mul_(0.02))
+    ring = measure.ring_count(n * k // 2 + n * k // 16)
+    packs = [(q.packed.clone(), q.scales.clone()) for _ in range(ring)]
+    x = bf16_normal((1, k), 1.0, 7)
+    out = torch.empty((1, n), dtype=torch.bfloat16, device=dev)
+    record("c3_fp4_e4m3g16_m1 (reference format)", 1, n, k, n * k // 2 + n * k // 16 + 4 + k * 2 + n * 2,
+           lambda i: fp4.fused_linear(x, packs[i][0], packs[i][1], q.global_scale, out=out,
+                                      output_dtype=torch.bfloat16), ring)
+    del packs, q
 
     # C4: lossless-coded BF16, 8 independent 4096 x 4096 layers
     n = k = 4096
@@ -240,8 +279,7 @@ def bench_projections(torch, peak, quick=False):
     storage = sum(c.storage_bytes for c in coded) / len(coded)
     nbytes = int(storage) + k * 2 + n * 2
     record("c4_lossless_bf16_m1", 1, n, k, nbytes,
-           lambda i: cb.fused_linear(x, coded[i], threads=128, vector=8, output_dtype="bf16", out=out),
-           lambda i: F.linear(x, raws[i % len(raws)]), ring)
+           lambda i: cb.fused_linear(x, coded[i], threads=128, vector=8, output_dtype="bf16", out=out), ring, x, raws)
     results[-1]["storage_fraction"] = round(storage / (n * k * 2), 4)
     results[-1]["effective_bf16_gbs"] = round((n * k * 2 + k * 2 + n * 2) / results[-1]["us"] / 1e3, 1)
     del coded, raws, layers
