@@ -82,8 +82,11 @@ extern "C" {
 #define KLAB_OPT_SPLIT 1      /* -1 (default) automatic, 0 never, 1 always (when workspace allows) */
 #define KLAB_OPT_GENERIC 2    /* 1: force the cooperative-load (non bulk-copy) fill path */
 #define KLAB_OPT_CTAS_PER_SM 3 /* cap on projection CTAs per SM (0, default: as many as fit) */
-#define KLAB_OPT_TENSOR 4      /* token tiles on tcgen05 tensor cores: 0 never, 1 (default) INT8 per-row
-                                  weights at M >= 16, 2 INT8 per-row and BF16 weights at M >= 2 */
+#define KLAB_OPT_TENSOR 4      /* tensor-core routes: 0 never (CUDA cores only); 1 (default) warp-level
+                                  tensor-core token tiles for INT8 per-row at M = 2..8 and E2M1/FP16-per-32
+                                  at M = 2..16 (BF16/FP16 x), INT8 per-row at M > 8 on tcgen05, M = 1 on the
+                                  CUDA cores; 2 INT8 per-row and BF16 weights at M >= 2 on tcgen05; 3 the
+                                  token tiles at every M <= 16 (results independent of M), tcgen05 above */
 #define KLAB_OPT_PROLOGUE 5    /* weight copies issued before the previous launch completes, per warp:
                                   (items into shared memory) + 16 * (items prefetched into L2);
                                   each part 0..3, -1 (default) the tuned choice */

@@ -33,7 +33,7 @@ NVCC_FLAGS = ARCH + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC", "-
                      "-fvisibility=hidden", f"-I{INCLUDE}"]
 CUDA_SOURCES = ("capi.cu", "aux_kernels.cu", "prefetch_kernels.cu", "gemv_half.cu", "gemv_cbf16.cu",
                 "gemv_int8.cu", "gemv_fp4a.cu", "gemv_fp4b.cu", "noalloc.cu", "peer.cu", "chain_kernel.cu",
-                "gemv_lossless.cu", "tc_gemm.cu", "decode_ops.cu", "decode_attn.cu")
+                "gemv_lossless.cu", "tc_gemm.cu", "tile_mma.cu", "decode_ops.cu", "decode_attn.cu")
 CXX_SOURCES = ("driver_abi.cpp", "codec_host.cpp")
 EXPORTS = OUT / "exports.map"
 

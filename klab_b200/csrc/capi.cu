@@ -39,10 +39,14 @@ std::atomic<int> g_opt_prologue{-1};
 // 4-token tiles with 16 warps beat one 8-token tile with 8 warps (config 3 M=8:
 // 63.3 -> 50.8 us; config 2 M=16 on CUDA cores: 111.7 -> 97.9 us).
 std::atomic<int> g_opt_max_tile{4};
-// Tensor-core path for token tiles: 0 off; 1 (default) INT8 per-row weights at
-// M >= 16, where the tile is a dense contraction; 2 INT8 per-row and BF16 weights
-// at M >= 2 (BF16 M-tiles then differ from M = 1 in the last bits; the
-// CUDA-core M-tiles are bit-identical to M = 1).
+// Tensor-core routes: 0 off (CUDA cores only); 1 (default) the fastest measured on B200:
+// the warp-level tensor-core token tiles (tile_mma.cu: one weight decode per token tile)
+// for INT8 per-row at 2 <= M <= 8 and E2M1/FP16-per-32 at 2 <= M <= 16 with BF16 or FP16
+// x, INT8 per-row at M > 8 on tcgen05, M = 1 on the CUDA cores; 2 INT8 per-row and BF16
+// weights at M >= 2 on tcgen05 (BF16 M-tiles then differ from M = 1 in the last bits; the
+// CUDA-core M-tiles are bit-identical to M = 1); 3 the token tiles for INT8 per-row and
+// E2M1 at every M <= 16 (a token's result then does not depend on M), INT8 per-row at
+// M > 16 on tcgen05.
 std::atomic<int> g_opt_tensor{1};
 
 struct DeviceInfo {
@@ -257,10 +261,20 @@ int run_gemv_multi(int wfmt, int xdt, const void* x, int ldx, int nseg, const vo
   // A fused elementwise op computes x while staging it: BF16 x and weights, K % 8 == 0.
   if (pro && (xdt != KLAB_DT_BF16 || (wfmt != W_BF16 && wfmt != W_CBF16) || k % 8 || gather))
     return KLAB_E_UNSUPPORTED;
-  // Token tiles of INT8 (and, optionally, BF16) weights go to the tensor cores.
   const int tensor = g_opt_tensor.load();
+  // INT8 per-row and E2M1/FP16-per-32 weights: warp-level tensor-core token tiles.
+  const int tile_max = tensor == 3 ? 16 : (wfmt == W_I8_ROW ? 8 : 16), tile_min = tensor == 3 ? 1 : 2;
+  if ((tensor == 1 || tensor == 3) && !plan_out && !pro && m >= tile_min && m <= tile_max && nseg == 1 && !gather &&
+      (xdt == KLAB_DT_BF16 || xdt == KLAB_DT_F16) && (wfmt == W_I8_ROW || wfmt == W_FP4_G32H)) {
+    const int rc_tm = tile_mma_launch(wfmt == W_I8_ROW ? 0 : 1, xdt == KLAB_DT_F16, x, ldx, w[0], aux[0], out[0],
+                                      ldo[0], out_dt == KLAB_DT_F32, m, nrows[0], k, ws, ws_bytes, info->sms,
+                                      info->status, g_opt_pdl.load() != 0, static_cast<cudaStream_t>(stream));
+    if (rc_tm != KLAB_E_ALIGN && rc_tm != KLAB_E_UNSUPPORTED) return rc_tm;  // else the CUDA cores
+  }
+  // Token tiles of INT8 (and, optionally, BF16) weights on tcgen05.
   if (!plan_out && !pro && m >= 2 && nseg == 1 && !gather && xdt == KLAB_DT_BF16 &&
-      ((wfmt == W_I8_ROW && (tensor == 2 || (tensor == 1 && m >= 16))) || (wfmt == W_BF16 && tensor == 2))) {
+      ((wfmt == W_I8_ROW && (tensor == 2 || (tensor == 1 && m > 8) || (tensor == 3 && m > 16))) ||
+       (wfmt == W_BF16 && tensor == 2))) {
     const int rc_tc = tc_gemm_launch(wfmt == W_I8_ROW ? 1 : 0, x, ldx, w[0], wfmt == W_I8_ROW ?
                                      static_cast<const float*>(aux[0]) : nullptr, out[0], ldo[0],
                                      out_dt == KLAB_DT_F32, m, nrows[0], k, info->status,
@@ -677,9 +691,11 @@ size_t klab_gemv_workspace_bytes(int wfmt, int m, int n, int k) {
   if (wfmt < W_BF16 || wfmt > W_FP28 || m <= 0 || n <= 0 || k <= 0) return 0;
   const int kc = 256 * vals_of(wfmt);
   const int chunks = (k + kc - 1) / kc;
-  if (chunks < 2 || static_cast<size_t>(n) > kTicketCap) return 0;
+  // The warp-level tensor-core token tiles keep phase partials of row groups split between CTAs.
+  size_t best = (m <= 16 && (wfmt == W_I8_ROW || wfmt == W_FP4_G32H))
+                    ? tile_mma_workspace(wfmt == W_I8_ROW ? 0 : 1, m, n, k) : 0;
+  if (chunks < 2 || static_cast<size_t>(n) > kTicketCap) return best;
   // Largest need over the tile choices the planner can make for this M.
-  size_t best = 0;
   for (int mt = tile_for(m); mt >= 1; mt /= 2) {
     const size_t need = workspace_need((m + mt - 1) / mt, mt, n, chunks);
     if (need > best) best = need;
@@ -756,7 +772,7 @@ int klab_set_option(int option, int value) {
       g_opt_ctas_per_sm.store(value);
       return 0;
     case KLAB_OPT_TENSOR:
-      if (value < 0 || value > 2) return KLAB_E_INVALID;
+      if (value < 0 || value > 3) return KLAB_E_INVALID;
       g_opt_tensor.store(value);
       return 0;
     case KLAB_OPT_PROLOGUE:

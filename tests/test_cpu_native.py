@@ -51,7 +51,7 @@ def test_error_strings_and_options():
     assert "Shape" in _native.error_string(_native.E_SHAPE)
     assert _native.lib().lab_error_string(-1000).decode().startswith("Cannot load CUDA driver")
     for opt, values in ((_native.OPT_SPLIT, (-1, 0, 1)), (_native.OPT_PDL, (0, 1)), (_native.OPT_GENERIC, (1, 0)),
-                        (_native.OPT_TENSOR, (0, 2, 1)), (_native.OPT_CTAS_PER_SM, (1, 0)),
+                        (_native.OPT_TENSOR, (0, 2, 3, 1)), (_native.OPT_CTAS_PER_SM, (1, 0)),
                         (_native.OPT_PROLOGUE, (0x00, 0x02, 0x10, 0x31, -1)), (_native.OPT_MAX_TILE, (8, 1, 2, 4))):
         before = _native.get_option(opt)
         for v in values:

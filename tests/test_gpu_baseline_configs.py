@@ -10,9 +10,9 @@ one BF16 ulp of the FP64 result rounded once; lossless-coded outputs equal to
 the raw BF16 projection of the same weights bit for bit; the 32-layer chain's
 first two layers (Llama-3-8B projection shapes) against FP64 with the chain's
 per-stage BF16 rounding, through the launch-per-stage chain and the persistent
-one-launch chain. Tensor-core token tiles (INT8 per-row, M >= 16) accumulate in
-the tensor core's FP32 order, so they are held to check_outputs; the same
-shape on the CUDA-core tiles is held to one ulp as well."""
+one-launch chain. INT8 per-row and E2M1 run on every route (the default choice,
+the warp-level tensor-core token tiles at every M, and the CUDA-core kernel), each
+held to one ulp."""
 
 import numpy as np
 import pytest
@@ -95,32 +95,32 @@ def test_c2_int8_per_row_14336x4096(native, c2_weights, m):
     gen = torch.Generator().manual_seed(m)
     x = normal((m, 4096), 1.0, gen).bfloat16()
     ref = og.projection64(ob.bf16_values(bits_of(x)), deq)
-    y = i8.fused_linear(x.cuda(), q.codes, q.scales, output_dtype=torch.bfloat16)   # the default route
-    report = ob.check_outputs(ref, y.float().cpu().numpy(), output_dtype="bf16")
-    assert report["passed"], report
-    if m < 16:
-        assert report["max_ulp_error"] <= 1, report
-    native.set_option(native.OPT_TENSOR, 0)                                        # CUDA-core tiles
-    try:
-        y_cc = i8.fused_linear(x.cuda(), q.codes, q.scales, output_dtype=torch.bfloat16)
-    finally:
-        native.set_option(native.OPT_TENSOR, 1)
-    assert_one_ulp(ref, y_cc, f"c2 m={m} cuda cores")
-    if m < 16:
-        assert same_bits(y_cc, y)
+    for route, name in ((1, "default route"), (3, "tensor-core token tile"), (0, "cuda cores")):
+        native.set_option(native.OPT_TENSOR, route)
+        try:
+            y = i8.fused_linear(x.cuda(), q.codes, q.scales, output_dtype=torch.bfloat16)
+        finally:
+            native.set_option(native.OPT_TENSOR, 1)
+        assert_one_ulp(ref, y, f"c2 m={m} {name}")
 
 
 # ---------------------------------------------------------------- config 3
 
 @pytest.mark.parametrize("m", [1, 8])
-def test_c3_fp4_f16_scale_8192x8192(c3_weights, m):
+def test_c3_fp4_f16_scale_8192x8192(native, c3_weights, m):
     """E2M1 weights, FP16 scale per 32 K (max|group|/6), nearest-E2M1, low nibble = even k;
     x ~ N(0, 1) BF16."""
     q, deq = c3_weights
     gen = torch.Generator().manual_seed(10 + m)
     x = normal((m, 8192), 1.0, gen).bfloat16()
-    y = q.linear(x.cuda(), output_dtype=torch.bfloat16)
-    assert_one_ulp(og.projection64(ob.bf16_values(bits_of(x)), deq), y, f"c3 m={m}")
+    ref = og.projection64(ob.bf16_values(bits_of(x)), deq)
+    for route, name in ((1, "default route"), (3, "tensor-core token tile"), (0, "cuda cores")):
+        native.set_option(native.OPT_TENSOR, route)
+        try:
+            y = q.linear(x.cuda(), output_dtype=torch.bfloat16)
+        finally:
+            native.set_option(native.OPT_TENSOR, 1)
+        assert_one_ulp(ref, y, f"c3 m={m} {name}")
 
 
 @pytest.fixture(scope="module")

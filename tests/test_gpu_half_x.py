@@ -6,7 +6,9 @@ fma.rn.f32.f16 on raw 16-bit pairs); otherwise the tile keeps BF16 staging and
 the FP32 path. Both paths must give the same bits: a token computed alone (FP16
 path) equals the same token inside a tile that a wide-range token forces onto
 the FP32 path. Scaling x by a power of two scales the FP32 output exactly, and
-wide-range, subnormal and non-finite tokens still meet the oracle's interval."""
+wide-range, subnormal and non-finite tokens still meet the oracle's interval.
+These are properties of the CUDA-core kernel: the module runs with the tensor-core
+token tiles switched off (KLAB_OPT_TENSOR 0)."""
 
 import numpy as np
 import pytest
@@ -26,7 +28,9 @@ def native():
     from klab_b200 import _native
 
     _native.lib()
+    _native.set_option(_native.OPT_TENSOR, 0)
     yield _native
+    _native.set_option(_native.OPT_TENSOR, 1)
     assert _native.device_status(clear=True) == 0, "a kernel recorded a device-side error"
 
 

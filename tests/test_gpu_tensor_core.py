@@ -71,4 +71,4 @@ def test_tensor_core_option_values(native):
     native.set_option(native.OPT_TENSOR, 2)
     assert native.get_option(native.OPT_TENSOR) == 2
     with pytest.raises(native.KlabError):
-        native.set_option(native.OPT_TENSOR, 3)
+        native.set_option(native.OPT_TENSOR, 4)
