@@ -10,6 +10,9 @@ native/cli.cpp:37-44 execs experiments.py, experiments.py:253-334 dispatches).
     klab run [problem] [--shape M,N,K] [--rounds R] [--seed S] [--output FILE] [--json]
                                            time one projection (or the chain) the way
                                            the benchmark does, beside cuBLAS
+    klab profile [problem] [--shape M,N,K] [--length L] [--calls C]
+                                           a few calls of one case on one weight set,
+                                           for a profiler (ncu -k ... -s/-c); not timed
     klab version | help [command]
 
 Exit status: 0 success, 1 a failed check or a runtime error, 2 a usage error
@@ -93,6 +96,12 @@ def parser():
     run.add_argument("--output", help="also write the JSON result to this file (under the working directory)")
     run.add_argument("--json", action="store_true")
     sub.add_parser("version")
+    prof = sub.add_parser("profile")
+    prof.add_argument("problem", nargs="?", default="bf16-projection", choices=list(_BY_ID))
+    prof.add_argument("--shape", help="M,N,K (projection problems)")
+    prof.add_argument("--length", type=int, default=4095, help="decode-step: cached tokens (capacity 4096)")
+    prof.add_argument("--calls", type=int, default=4)
+    prof.add_argument("--seed", type=int, default=1)
     helper = sub.add_parser("help")
     helper.add_argument("topic", nargs="?")
     return p
@@ -298,6 +307,72 @@ def cmd_run(args):
     return 0
 
 
+def _profile_case(problem, shape, length, seed):
+    """A zero-argument callable running one call of the case: seeded synthetic weights and
+    activations with the benchmark configs' distributions (W ~ N(0, 0.02^2), x ~ N(0, 1)), one
+    weight set, so a profiler captures the kernel without rings of copies around it."""
+    import torch
+
+    from . import compressed_bf16 as cb
+    from . import fp4, int8_weights
+
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+
+    def normal(dims, std=1.0):
+        return torch.randn(dims, generator=gen, device="cuda").mul_(std)
+
+    if problem == "decode-step":
+        from .decode_attn import decode_attention
+
+        if not 0 <= length < 4096:
+            raise UsageError("--length must be in [0, 4096)")
+        kc, vc = normal((8, 4096, 64)).to(torch.bfloat16), normal((8, 4096, 64)).to(torch.bfloat16)
+        q, kn, vn = (normal((n,)).to(torch.bfloat16) for n in (32 * 64, 8 * 64, 8 * 64))
+        return lambda: decode_attention(q, kn, vn, kc, vc, length)
+    m, n, k = shape
+    x = normal((m, k)).to(torch.bfloat16)
+    w32 = normal((n, k), 0.02)
+    if problem == "bf16-projection":
+        w = w32.to(torch.bfloat16)
+        return lambda: cb.raw_linear(x, w, threads=128, vector=8, output_dtype="bf16")
+    if problem == "lossless-bf16-projection":
+        if k % 64:
+            raise UsageError("lossless-bf16-projection needs K % 64 == 0")
+        packed = cb.upload(cb.pack_bits(w32.to(torch.bfloat16).view(torch.int16).cpu().numpy().view("uint16")), "cuda")
+        return lambda: cb.fused_linear(x, packed, threads=128, vector=8, output_dtype="bf16")
+    if problem == "int8-projection":
+        q = int8_weights.quantize_weights_per_row(w32)
+        return lambda: int8_weights.fused_linear(x, q.codes, q.scales, output_dtype=torch.bfloat16)
+    if problem == "fp4-projection":
+        if k % 32:
+            raise UsageError("fp4-projection needs K % 32 == 0")
+        q = fp4.quantize_weights_f16(w32)
+        return lambda: q.linear(x, output_dtype=torch.bfloat16)
+    raise UsageError(f"klab profile does not run {problem}")
+
+
+def cmd_profile(args):
+    problem = _BY_ID[args.problem]
+    if args.calls < 1:
+        raise UsageError("--calls must be at least 1")
+    if args.problem not in ("bf16-projection", "int8-projection", "fp4-projection", "lossless-bf16-projection",
+                            "decode-step"):
+        raise UsageError(f"klab profile does not run {args.problem}")
+    shape = None if args.problem == "decode-step" else _shape(args.shape, problem["default_shape"])
+    if shape is None and not 0 <= args.length < 4096:
+        raise UsageError("--length must be in [0, 4096)")
+    import torch
+
+    if not torch.cuda.is_available():
+        raise RuntimeError("CUDA is unavailable; klab profile runs the GPU path")
+    fn = _profile_case(args.problem, shape, args.length, args.seed)
+    for _ in range(args.calls):
+        fn()
+    torch.cuda.synchronize()
+    print("ok", args.problem, "x".join(map(str, shape)) if shape else f"length {args.length}", f"{args.calls} calls")
+    return 0
+
+
 def main(argv=None):
     argv = list(sys.argv[1:] if argv is None else argv)
     if not argv or argv in (["--help"], ["-h"]):
@@ -323,7 +398,7 @@ def main(argv=None):
                 sub.print_help()
             return 0
         handler = {"problems": cmd_problems, "show": cmd_show, "doctor": cmd_doctor, "check": cmd_check,
-                   "verify": cmd_check, "run": cmd_run, "bench": cmd_run}[args.command]
+                   "verify": cmd_check, "run": cmd_run, "bench": cmd_run, "profile": cmd_profile}[args.command]
         return handler(args)
     except UsageError as error:
         print(f"klab: {error}", file=sys.stderr)

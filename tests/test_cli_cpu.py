@@ -43,7 +43,9 @@ def test_version_problems_and_help_need_no_gpu():
 
 @pytest.mark.parametrize("args", [("run", "--output", "../escape.json"), ("run", "--output", "/tmp/x.json"),
                                   ("run", "--output", "results/notes.md"), ("run", "--shape", "1,2"),
-                                  ("nonsense",), ("run", "no-such-problem")])
+                                  ("nonsense",), ("run", "no-such-problem"), ("profile", "--shape", "1,2"),
+                                  ("profile", "int8-projection", "--calls", "0"), ("profile", "projection-chain"),
+                                  ("profile", "decode-step", "--length", "4096")])
 def test_usage_errors_exit_2_before_any_gpu_work(args):
     r = run(*args)
     assert r.returncode == 2, (r.stdout, r.stderr)

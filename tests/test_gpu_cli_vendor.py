@@ -95,3 +95,11 @@ def test_frozen_cublaslt_plan_round_trip(m, n, k, out):
     assert report["passed"], report
     with pytest.raises(ValueError):
         lt.validate_frozen(record, lt.runtime_context(x.device, x.dtype, out, m + 1, n, k))
+
+
+@pytest.mark.parametrize("args", [("int8-projection", "--shape", "4,1000,2048"), ("fp4-projection", "--shape", "8,512,4096"),
+                                  ("lossless-bf16-projection", "--shape", "1,256,1024"), ("decode-step", "--length", "300")])
+def test_klab_profile_runs_a_case(args):
+    from klab_b200 import cli
+
+    assert cli.main(["profile", *args, "--calls", "2"]) == 0
