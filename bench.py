@@ -570,6 +570,8 @@ def main(argv=None):
     parser.add_argument("--quick", action="store_true", help="fewer rounds and shapes (smoke runs)")
     parser.add_argument("--gather", choices=("nccl", "p2p"), default="p2p",
                         help="N>1: NCCL all-gathers, or gathers fused into the projections over NVLink")
+    parser.add_argument("--stages-per-layer", type=int, choices=(2, 4), default=2,
+                        help="persistent chain: stages per layer (ProjectionChain.persistent_schedule)")
     parser.add_argument("--persistent", action=argparse.BooleanOptionalAction, default=None,
                         help="the whole token step as one persistent kernel launch "
                              "(default: with several GPUs; one launch per stage on one GPU)")
@@ -603,7 +605,7 @@ def main(argv=None):
     peak, peak_kind = measured_peak()
     shape = ChainShape(layers=args.layers)
     chain = ProjectionChain(shape, rank=rank, world=world, group=group, seed=0, gather=args.gather,
-                            persistent=args.persistent)
+                            persistent=args.persistent, stages_per_layer=args.stages_per_layer)
     gen = torch.Generator(device="cuda")
     gen.manual_seed(1234)
     x = torch.randn((1, shape.hidden), generator=gen, device="cuda").to(torch.bfloat16)

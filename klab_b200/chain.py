@@ -105,13 +105,16 @@ class ProjectionChain:
     process group (NCCL) when world > 1."""
 
     def __init__(self, shape: ChainShape = ChainShape(), *, rank=0, world=1, device=None, group=None,
-                 seed=0, std=0.02, weights=None, project=None, fuse=True, gather="nccl", persistent=False):
+                 seed=0, std=0.02, weights=None, project=None, fuse=True, gather="nccl", persistent=False,
+                 stages_per_layer=2):
         """weights(layer, name, rows) -> BF16 tensor supplies shard weights (default:
         seeded N(0, std^2)); project(x, w, n_rows, k, out, ldo) replaces the native
         projection (host-side tests drive the sharding and gathers on CPU with it).
         gather: "nccl" or "p2p" (fused peer stores; needs the native fused path).
         persistent: the whole step is one launch of the persistent chain kernel
-        (one token; with world > 1 it needs gather="p2p")."""
+        (one token; with world > 1 it needs gather="p2p"); stages_per_layer: 2 or 4
+        stages of the persistent kernel per layer (persistent_schedule; 2, the
+        default, measured faster on B200 at 2, 4 and 8 ranks)."""
         if gather not in ("nccl", "p2p"):
             raise ValueError(f"gather must be 'nccl' or 'p2p', not {gather!r}")
         if gather == "p2p" and (project is not None or not fuse):
@@ -120,7 +123,10 @@ class ProjectionChain:
                            or (world > 1 and gather != "p2p")):
             raise ValueError("persistent=True needs the native projection, fuse=True, one token and, "
                              "with several ranks, gather='p2p'")
+        if stages_per_layer not in (2, 4):
+            raise ValueError("stages_per_layer must be 2 or 4")
         self.persistent = persistent
+        self.stages_per_layer = stages_per_layer
         self._plan = None
         if world > 8 and gather == "p2p":
             raise ValueError("gather='p2p' supports at most 8 ranks")
@@ -169,18 +175,27 @@ class ProjectionChain:
             self._setup_persistent()
 
     def persistent_schedule(self):
-        """Stages of the persistent kernel for one layer i, in order:
-        up (gathered into up_t; x = h_i), fill1 (first half of q, k, v, o, gate
-        rows; x = h_i), down (gathered into h_t[(i+1) % 2]; x = up_t), fill2
-        (the other half; x = h_i again). Only up and down feed later stages, so
-        each data dependency (up -> down, down -> next up) has a filler stage of
-        independent rows between producer and consumer. Returns, per layer, a
-        list of (kind, [(name, local_row_begin, local_row_end)])."""
+        """Stages of the persistent kernel for one layer i, in order. Every CTA takes
+        an equal share of a stage's rows in at most two contiguous parts: of a
+        gathered segment listed first, then of the other rows, so the gathered rows
+        are produced first everywhere while the stage's other rows hide their
+        gather. Only up and down feed later stages.
+
+        stages_per_layer=2 (default): "up" = [up (gathered into up_t), q, k, v, o,
+        gate] (x = h_i); "down" = [down] (gathered into h_t[(i+1) % 2]; x = up_t).
+        stages_per_layer=4: up; fill1 (first half of the q, k, v, o, gate rows;
+        x = h_i); down; fill2 (the other half; x = h_i again): a filler stage
+        between each producer and consumer, at twice the stage boundaries.
+        Measured on B200 (tok/s, 2 / 4 / 8 GPUs): 2 stages 773.7 / 1,207.8 /
+        1,567.9; 4 stages 719.5 / 1,052.0 / 1,366.4.
+        Returns, per layer, a list of (kind, [(name, local_row_begin, local_row_end)])."""
         names = [name for name, _ in self.shape.projections()[0] if name != "up"]
         fill = []
         for name in names:
             n = self.layers[0][name][1][1] - self.layers[0][name][1][0]
             fill.append((name, 0, n))
+        if self.stages_per_layer == 2:
+            return [("up", [("up", 0, None)] + fill), ("down", [("down", 0, None)])]
         total = sum(e - b for _, b, e in fill)
         half, fill1, fill2, acc = total // 2, [], [], 0
         for name, b, e in fill:
@@ -227,10 +242,15 @@ class ProjectionChain:
                 st.gather_seg = -1
                 if kind == "up":
                     w, rows, _ = entry["up"]
-                    st.x, st.k, st.x_stage, st.nseg, st.gather_seg = h_ptr, shape.hidden, prev_down, 1, 0
+                    st.x, st.k, st.x_stage, st.nseg, st.gather_seg = h_ptr, shape.hidden, prev_down, len(parts), 0
                     st.w[0], st.n[0] = w.data_ptr(), rows[1] - rows[0]
                     for q in range(world):
                         st.peer_out[q] = bases["upt"][q] + rows[0] * 4
+                    for j, (name, b, e) in enumerate(parts[1:], start=1):   # rows that also read h_i
+                        w, rows, _ = entry[name]
+                        st.w[j] = w[b:].data_ptr()
+                        st.out[j] = self.a_out[name][:, rows[0] + b:].data_ptr()
+                        st.n[j] = e - b
                     up_stage = len(stages)
                 elif kind == "down":
                     w, rows, _ = entry["down"]
@@ -262,8 +282,7 @@ class ProjectionChain:
         """Run one eager step of the persistent kernel with its timeline on and
         return it as an int64 tensor [stages, CTAs, slots] of global-timer ns
         (slots: entered, previous stage done in this CTA, x staged, then per
-        warp: first item of the stage landed, run computed, done after its
-        deferred fold)."""
+        warp: first item of the stage landed, run computed, done)."""
         if not self.persistent:
             raise ValueError("trace_step needs persistent=True")
         grid, slots = _native.chain_info(self._plan)

@@ -5,16 +5,20 @@
 // each with a private ring of kChainDepth bulk-copy slots (one slot = one row x
 // 4 KiB chunk of weights = one "item").
 //
-// Work: each stage's n*S items are dealt to the warps as contiguous runs of
-// equal length (no atomics). A warp's lane 0 issues its next item as soon as a
-// slot is consumed, running on into the next stage's run, so the weight stream
-// of stage s+1 is in flight while the stage-s data dependency is still being
-// resolved (weights never depend on activations). Rows inside one run are
-// folded in registers. A row cut by a run boundary publishes tagged per-chunk
-// partials (64-bit words: tag << 32 | fp32 bits); the warp whose run holds the
-// row's last chunk folds them after the rest of its run, polling for the tags
-// (at most one such row per warp and stage), so no warp ever waits in the
-// middle of its run and no tickets, atomics or fences are needed.
+// Work: every CTA takes an equal share of a stage's rows in at most two
+// contiguous parts (the gathered segment first when a stage lists it first with
+// other rows, so it is produced first everywhere), and a CTA's items (its rows x
+// S chunks) go to its warps as contiguous runs of equal length (no atomics
+// across CTAs). A warp's lane 0 issues its next item as soon
+// as a slot is consumed, running on into the next stage's run, so the weight
+// stream of stage s+1 is in flight while the stage-s data dependency is still
+// being resolved (weights never depend on activations). Rows inside one run are
+// folded in registers. A row cut by a warp-run boundary lies inside one CTA: its
+// contributors put their chunk partials in a shared-memory slot and add their
+// chunk count to the slot's counter; the one that completes the count folds the
+// partials in chunk order at once and clears the counter. No warp waits on
+// another CTA except through the gathered inputs, which are the true data
+// dependencies.
 //
 // Data exchange: the outputs that later stages read (the gathered segment of a
 // stage) are written as 32-bit words (tag << 16 | bf16) into every rank's copy
@@ -70,7 +74,6 @@ struct ChainSeg {
 struct ChainStage {
   const void* x;         // plain BF16 [k] (x_stage < 0) or tagged words [k]
   int k, chunks, n, nseg;
-  long long ws_off;      // this stage's tagged partials [n][S] (64-bit words)
   int gather_seg;        // segment written as tagged words to every rank (-1: none)
   int x_stage;           // stage whose gathered output x is (-1: plain input)
   ChainSeg seg[kMaxSegs];
@@ -83,7 +86,6 @@ struct ChainParams {
   int npeers, rank;
   unsigned* epoch;                 // completed steps (this rank)
   unsigned* exits;                 // CTAs finished with the step, zero between steps
-  unsigned long long* ws;          // tagged split-row partials
   int* status;
   const unsigned* final_in;        // tagged output of stage final_stage
   unsigned short* final_out;       // its BF16 values
@@ -94,7 +96,7 @@ struct ChainParams {
 
 // Trace slots per (stage, CTA): entered, every warp done with the previous
 // stage, x staged, then per warp: its first item of the stage landed, its run
-// computed, and done (after folding its deferred row).
+// computed, and done.
 constexpr int kTraceCta = 3;
 constexpr int kTraceWarp = 3;
 constexpr int kTraceSlots = kTraceCta + kTraceWarp * kChainWarps;
@@ -118,16 +120,6 @@ __device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
   return v;
 }
 
-__device__ __forceinline__ unsigned long long ld_relaxed_gpu_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_relaxed_gpu_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
 // Tag of stage s's outputs in step `epoch` (never 0, the value of a fresh buffer).
 __device__ __forceinline__ unsigned stage_tag(unsigned epoch, int nstages, int s) {
   return 1u + (epoch * static_cast<unsigned>(nstages) + static_cast<unsigned>(s)) % 65535u;
@@ -141,26 +133,73 @@ __device__ __forceinline__ int seg_of(const ChainStage& st, int row) {
   return s;
 }
 
-// This warp's contiguous run [begin, end) of a stage's n*S items.
+// Rows of segment i of a stage.
+__device__ __forceinline__ int seg_rows(const ChainStage& st, int i) {
+  return (i + 1 < st.nseg ? st.seg[i + 1].row0 : st.n) - st.seg[i].row0;
+}
+
+// CTA b's share of a stage, in two contiguous parts so that a CTA touches few weight pages
+// (a warp's first access to a page whose translation is not cached stalls it ~1 us): part 1
+// is the gathered segment when it is segment 0 of a stage with other segments (CTA b takes
+// rows [n1 b / G, n1 (b + 1) / G) of it first, so those rows are produced first everywhere),
+// part 2 the stage's other rows (rows [n1 + n2 b / G, n1 + n2 (b + 1) / G)). "Local rows"
+// number the share in that order.
+__device__ __forceinline__ int first_part_rows(const ChainStage& st) {
+  return (st.gather_seg == 0 && st.nseg > 1) ? seg_rows(st, 0) : 0;
+}
+
+// 32-bit arithmetic throughout: rows x CTAs and items x 16 stay below 2^31 (checked at plan
+// creation), and these run on the issue path of every row.
+__device__ __forceinline__ int share_rows(const ChainStage& st, unsigned b, unsigned G) {
+  const unsigned n1 = static_cast<unsigned>(first_part_rows(st)), n2 = static_cast<unsigned>(st.n) - n1;
+  return static_cast<int>(n1 * (b + 1) / G - n1 * b / G + n2 * (b + 1) / G - n2 * b / G);
+}
+
+// CTA b's share as (first part: rows lo1 .. lo1 + c1 - 1; then rows from base2), computed once
+// per stage; row(lr) is the stage row of local row lr.
+struct Share {
+  int lo1, c1, base2;
+  __device__ __forceinline__ void set(const ChainStage& st, unsigned b, unsigned G) {
+    const unsigned n1 = static_cast<unsigned>(first_part_rows(st)), n2 = static_cast<unsigned>(st.n) - n1;
+    lo1 = static_cast<int>(n1 * b / G);
+    c1 = static_cast<int>(n1 * (b + 1) / G) - lo1;
+    base2 = static_cast<int>(n1 + n2 * b / G);
+  }
+  __device__ __forceinline__ int row(int lr) const { return lr < c1 ? lo1 + lr : base2 + (lr - c1); }
+};
+
+// This warp's contiguous run [begin, end) of its CTA's local items (local row x S + chunk).
 __device__ __forceinline__ void warp_range(const ChainStage& st, unsigned gw, unsigned nw, long long* begin,
                                            long long* end) {
-  const long long T = static_cast<long long>(st.n) * st.chunks;
-  *begin = T * gw / nw;
-  *end = T * (gw + 1) / nw;
+  const unsigned T = static_cast<unsigned>(share_rows(st, gw / kChainWarps, nw / kChainWarps) * st.chunks);
+  const unsigned w = gw % kChainWarps;
+  *begin = T * w / kChainWarps;
+  *end = T * (w + 1) / kChainWarps;
+}
+
+// Shared-memory slot of a row cut by warp-run boundaries: the first warp whose run begins
+// inside the row (local item index L of its first chunk, T items in the CTA), in 1..15.
+// Distinct cut rows have distinct first boundaries.
+__device__ __forceinline__ int cut_slot(long long L, long long T) {
+  const unsigned l = static_cast<unsigned>(L), t = static_cast<unsigned>(T);
+  return static_cast<int>((kChainWarps * (l + 1) + t - 1) / t);
 }
 
 // Issue side of one warp's item sequence over all stages (lane 0 only).
 struct IssueCursor {
-  int stage, row, c;
-  long long left;  // items left in this stage's run
+  int stage, lr, c, row;  // local row, chunk, and the local row's stage row
+  Share share;            // this CTA's share of `stage`
+  long long left;         // items left in this stage's run
   __device__ __forceinline__ void enter(const ChainParams& p, unsigned gw, unsigned nw, int s) {
     for (stage = s; stage < p.nstages; ++stage) {
       long long b, e;
       warp_range(p.stages[stage], gw, nw, &b, &e);
       if (e > b) {
         const int S = p.stages[stage].chunks;
-        row = static_cast<int>(b / S);
-        c = static_cast<int>(b - static_cast<long long>(row) * S);
+        lr = static_cast<int>(b / S);
+        c = static_cast<int>(b - static_cast<long long>(lr) * S);
+        share.set(p.stages[stage], gw / kChainWarps, nw / kChainWarps);
+        row = share.row(lr);
         left = e - b;
         return;
       }
@@ -181,7 +220,7 @@ struct IssueCursor {
       enter(p, gw, nw, stage + 1);
     } else if (++c == st.chunks) {
       c = 0;
-      ++row;
+      row = share.row(++lr);
     }
   }
 };
@@ -263,45 +302,11 @@ __device__ bool stage_chain_x(const ChainStage& st, bool tagged, unsigned tag, u
   return ok;
 }
 
-// Fold of a split row: poll its S tagged partials (bounded by time), add them
-// in chunk order and finalize. Lane 0 only.
-__device__ __forceinline__ void fold_split_row(const ChainParams& p, const ChainStage& st, int row, unsigned tag,
-                                               int* broken) {
-  const int S = st.chunks;
-  const unsigned long long* part = p.ws + st.ws_off + static_cast<long long>(row) * S;
-  unsigned long long w[kChainMaxS];
-#pragma unroll
-  for (int cc = 0; cc < kChainMaxS; ++cc) w[cc] = cc < S ? ld_relaxed_gpu_u64(part + cc) : 0ull;
-  const unsigned long long t0 = global_ns();
-  for (;;) {
-    bool all = true;
-#pragma unroll
-    for (int cc = 0; cc < kChainMaxS; ++cc)
-      if (cc < S && static_cast<unsigned>(w[cc] >> 32) != tag) all = false;
-    if (all) break;
-    if (*reinterpret_cast<volatile int*>(broken) || global_ns() - t0 > kChainWaitNs) {
-      *reinterpret_cast<volatile int*>(broken) = 1;
-      record_status(p.status, kStatusFlagTimeout);
-      break;
-    }
-    __nanosleep(32);
-#pragma unroll
-    for (int cc = 0; cc < kChainMaxS; ++cc)
-      if (cc < S && static_cast<unsigned>(w[cc] >> 32) != tag) w[cc] = ld_relaxed_gpu_u64(part + cc);
-  }
-  float v[kChainMaxS];
-#pragma unroll
-  for (int cc = 0; cc < kChainMaxS; ++cc) v[cc] = __uint_as_float(static_cast<unsigned>(w[cc]));
-  float total = v[0];
-#pragma unroll
-  for (int cc = 1; cc < kChainMaxS; ++cc)
-    if (cc < S) total = add_rn(total, v[cc]);
-  chain_finalize(p, st, row, total, tag);
-}
-
 __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ int s_broken;
+  __shared__ float s_part[kChainWarps][kChainMaxS];   // cut rows' chunk partials, by slot
+  __shared__ int s_count[kChainWarps];                 // chunks stored per slot (0 between stages)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const unsigned gw = blockIdx.x * kChainWarps + warp, nw = gridDim.x * kChainWarps;
   const unsigned pbar0 = smem_addr(smem) + warp * kChainDepth * 8;
@@ -309,6 +314,7 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
   unsigned char* xs = smem + kChainBarBytes + kChainWarps * kChainDepth * kChainSlot;
   const unsigned xs_lane0 = smem_addr(xs) + lane * 16;
   if (threadIdx.x == 0) s_broken = 0;
+  if (threadIdx.x < kChainWarps) s_count[threadIdx.x] = 0;
 
   // Ring prologue: the first kChainDepth items of this warp's sequence.
   IssueCursor iss{};
@@ -355,16 +361,17 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
     if (threadIdx.x == 0) trace_mark(p, s, 2);
     const unsigned tag = stage_tag(epoch, p.nstages, s);
 
-    int row = 0, c = 0;
+    int lr = 0, c = 0, row = 0;   // local row, chunk, stage row
     if (nitems > 0) {
-      row = static_cast<int>(wbegin / S);
-      c = static_cast<int>(wbegin - static_cast<long long>(row) * S);
+      lr = static_cast<int>(wbegin / S);
+      c = static_cast<int>(wbegin - static_cast<long long>(lr) * S);
     }
-    // The row cut by this run's start whose last chunk lies in this run is
-    // folded after the run (its earlier chunks come from preceding warps).
-    int deferred = -1;
+    const long long cta_items = static_cast<long long>(share_rows(st, blockIdx.x, gridDim.x)) * S;
+    Share share;
+    share.set(st, blockIdx.x, gridDim.x);
     float rowsum = 0.0f;
     bool whole = true;
+    int cut = 0, mine = 0;  // a cut row: its shared-memory slot, chunks this warp stored
     for (int q = 0; q < nitems; ++q, ++g) {
       const int L = min(kChainKC, k - c * kChainKC);
       const unsigned slot = slot0 + static_cast<unsigned>(g % kChainDepth) * kChainSlot;
@@ -388,24 +395,40 @@ __global__ void __launch_bounds__(kChainWarps * 32, 1) chain_kernel(const ChainP
           ++issued;
         }
       }
-      if (c == 0 || q == 0)
-        whole = static_cast<long long>(row) * S >= wbegin && static_cast<long long>(row) * S + S <= wend;
+      if (c == 0 || q == 0) {
+        row = share.row(lr);
+        whole = static_cast<long long>(lr) * S >= wbegin && static_cast<long long>(lr) * S + S <= wend;
+        if (!whole) {
+          cut = cut_slot(static_cast<long long>(lr) * S, cta_items);
+          mine = 0;
+        }
+      }
       if (whole) {
         rowsum = (c == 0) ? P[0] : add_rn(rowsum, P[0]);
         if (c == S - 1 && lane == 0) chain_finalize(p, st, row, rowsum, tag);
       } else {
-        if (lane == 0)
-          st_relaxed_gpu_u64(p.ws + st.ws_off + static_cast<long long>(row) * S + c,
-                             (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(P[0]));
-        if (c == S - 1) deferred = row;
+        ++mine;
+        if (lane == 0) {
+          s_part[cut][c] = P[0];
+          if (c == S - 1 || q == nitems - 1) {   // this warp's last chunk of the row
+            __threadfence_block();
+            if (atomicAdd(&s_count[cut], mine) + mine == S) {   // every chunk is in: fold in chunk order
+              __threadfence_block();
+              const volatile float* part = s_part[cut];
+              float total = part[0];
+              for (int cc = 1; cc < S; ++cc) total = add_rn(total, part[cc]);
+              chain_finalize(p, st, row, total, tag);
+              s_count[cut] = 0;
+            }
+          }
+        }
       }
       if (++c == S) {
         c = 0;
-        ++row;
+        ++lr;
       }
     }
     if (lane == 0) trace_mark(p, s, kTraceCta + kTraceWarp * warp + 1);
-    if (deferred >= 0 && lane == 0) fold_split_row(p, st, deferred, tag, &s_broken);
     if (lane == 0) trace_mark(p, s, kTraceCta + kTraceWarp * warp + 2);
   }
 
@@ -468,7 +491,6 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
     return KLAB_E_INVALID;
   if (!sync->final_in || (reinterpret_cast<uintptr_t>(sync->final_in) & 3)) return KLAB_E_INVALID;
   std::vector<ChainStage> host(nstages);
-  long long ws_words = 0;
   for (int s = 0; s < nstages; ++s) {
     const klab_chain_stage_t& in = stages[s];
     ChainStage& st = host[s];
@@ -504,8 +526,6 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
       st.peer_out[q] = static_cast<unsigned*>(in.peer_out[q]);
     }
     st.n = rows;
-    st.ws_off = ws_words;
-    ws_words += static_cast<long long>(rows) * st.chunks;
   }
 
   int dev = 0, sms = 0;
@@ -519,12 +539,19 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
   err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kChainWarps * 32, kChainSmem);
   if (err != cudaSuccess) return err;
   if (per_sm < 1) return KLAB_E_UNSUPPORTED;
-  // Every CTA holds items of every stage, so no CTA can still be reading a
-  // gather buffer when a later stage rewrites it (the rewriting stage's input
-  // is only complete once every CTA has passed the reading stages).
+  // Every CTA holds rows of every stage (its share of each segment, share_rows),
+  // so no CTA can still be reading a gather buffer when a later stage rewrites it
+  // (the rewriting stage's input is only complete once every CTA has passed the
+  // reading stages).
   int final_stage = -1;
   for (int s = 0; s < nstages; ++s) {
-    if (static_cast<long long>(host[s].n) * host[s].chunks < sms) return KLAB_E_SHAPE;
+    if (static_cast<long long>(host[s].n) * sms >= (1LL << 31) ||
+        static_cast<long long>(host[s].n) * host[s].chunks * kChainWarps >= (1LL << 31))
+      return KLAB_E_SHAPE;   // the kernel's 32-bit share arithmetic
+    const long long n1 = (host[s].gather_seg == 0 && host[s].nseg > 1) ? host[s].seg[1].row0 : 0;
+    const long long n2 = host[s].n - n1;
+    for (int b = 0; b < sms; ++b)
+      if (n1 * (b + 1) / sms - n1 * b / sms + n2 * (b + 1) / sms - n2 * b / sms < 1) return KLAB_E_SHAPE;
     if (host[s].gather_seg >= 0) final_stage = s;
   }
   if (final_stage < 0) return KLAB_E_INVALID;
@@ -532,8 +559,8 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
   ChainPlan* plan = new ChainPlan();
   plan->grid = sms;
   const size_t stage_bytes = sizeof(ChainStage) * nstages;
-  // [exit count][tagged partials]; partials never need clearing (tags).
-  const size_t total = 256 + static_cast<size_t>(ws_words) * 8;
+  // The CTA exit count (zero between steps).
+  const size_t total = 256;
   err = cudaMalloc(reinterpret_cast<void**>(&plan->d_stages), stage_bytes);
   if (err == cudaSuccess) err = cudaMemcpy(plan->d_stages, host.data(), stage_bytes, cudaMemcpyHostToDevice);
   if (err == cudaSuccess) err = cudaMalloc(&plan->d_ws, total);
@@ -552,7 +579,6 @@ KLAB_API int klab_chain_create(const klab_chain_stage_t* stages, int nstages, co
   p.rank = sync->rank;
   p.epoch = sync->epoch;
   p.exits = reinterpret_cast<unsigned*>(base);
-  p.ws = reinterpret_cast<unsigned long long*>(base + 256);
   p.status = device_status_address();
   p.final_in = sync->final_in;
   p.final_out = static_cast<unsigned short*>(sync->final_out);

@@ -464,8 +464,9 @@ def test_chain_fused_equals_unfused_and_graph():
     assert report["passed"] and report["max_ulp_error"] <= 1, report
 
 
+@pytest.mark.parametrize("stages_per_layer", [2, 4])
 @pytest.mark.parametrize("dims", [(3, 512, 128, 1536), (2, 1024, 256, 3584), (2, 256, 64, 512)])
-def test_persistent_chain_equals_launch_chain(native, dims):
+def test_persistent_chain_equals_launch_chain(native, dims, stages_per_layer):
     """The one-launch persistent chain (stage flags as a grid barrier, split rows
     folded in chunk order) gives the launch-per-stage chain's bits, eagerly and
     under graph replay, every step; every stage's local outputs match too."""
@@ -477,7 +478,7 @@ def test_persistent_chain_equals_launch_chain(native, dims):
     ref_chain = ProjectionChain(shape, seed=4)
     ref = ref_chain.forward_eager(x).clone()
     ref_a = {k: v.clone() for k, v in ref_chain.a_out.items()}
-    pc = ProjectionChain(shape, seed=4, persistent=True)
+    pc = ProjectionChain(shape, seed=4, persistent=True, stages_per_layer=stages_per_layer)
     assert pc.launches_per_step() == 1
     for _ in range(2):
         got = pc.forward_eager(x)
@@ -508,7 +509,7 @@ def test_persistent_chain_timeline(native):
     tr = pc.trace_step(x).numpy()
     assert same_bits(pc.forward_eager(x), ref)
     stages, grid, slots = tr.shape
-    assert stages == 4 * shape.layers and slots == 3 + 3 * 16
+    assert stages == len(pc.persistent_schedule()) * shape.layers and slots == 3 + 3 * 16
     assert (tr[:, :, :3] > 0).all()
     assert (tr[:, :, 0] <= tr[:, :, 1]).all() and (tr[:, :, 1] <= tr[:, :, 2]).all()
     first, run, done = tr[:, :, 3::3], tr[:, :, 4::3], tr[:, :, 5::3]
