@@ -58,12 +58,12 @@ def test_klab_run_and_check_end_to_end(tmp_path):
 
     klab = build_launcher()
     r = subprocess.run([str(klab), "run", "bf16-projection", "--shape", "1,2048,4096", "--rounds", "3", "--json",
-                        "--output", "gpurun_out/klab_run_test.json"], cwd=ROOT, capture_output=True, text=True,
+                        "--output", "results/klab_run_test.json"], cwd=tmp_path, capture_output=True, text=True,
                        timeout=600)
     assert r.returncode == 0, r.stderr
     row = json.loads(r.stdout)
     assert row["shape_mnk"] == [1, 2048, 4096] and row["us"] > 0 and row["cublas_us"] > 0
-    assert json.loads((ROOT / "gpurun_out" / "klab_run_test.json").read_text())["us"] == row["us"]
+    assert json.loads((tmp_path / "results" / "klab_run_test.json").read_text())["us"] == row["us"]
     r = subprocess.run([str(klab), "check", "fp4-projection", "--json"], cwd=ROOT, capture_output=True, text=True,
                        timeout=900)
     assert r.returncode == 0, (r.stdout, r.stderr)
