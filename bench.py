@@ -533,6 +533,40 @@ def chain_parity(torch):
             "against": "FP64 oracle, check_outputs interval + <= 1 bf16 ulp"}
 
 
+def chain_timeline(tr, per_layer, kinds):
+    """Summary of one traced persistent step, tr [stages, CTAs, slots] of global-timer ns
+    (slots: entered, previous stage done in the CTA, x staged, then per warp: first item
+    landed, run computed, done). Layer 0 is left out (cold). Per stage kind, medians over
+    stages and CTAs: barrier (entered -> every warp done with the previous stage), staging
+    (-> x staged, including the wait for a gathered input), first_wait (staged -> a warp's
+    first item landed), run (-> its last item computed), cta_span (staged -> the CTA's last
+    warp done), enter_skew (first to last CTA entering the stage); per layer: time, and the
+    spread of per-CTA busy time (staged -> last warp done, summed over the layer)."""
+    import numpy as np
+
+    stages, ctas, _ = tr.shape
+    layers = stages // per_layer
+    if layers < 2:
+        return None
+    out = {"per_layer_us": round(float((tr[-1, :, 5::3].max() - tr[per_layer, :, 0].min()) / 1e3 / (layers - 1)), 2)}
+    busy = np.zeros(ctas)
+    rows = {}
+    for s in range(per_layer, stages):
+        e, b, x_ = tr[s, :, 0], tr[s, :, 1], tr[s, :, 2]
+        first, run, done = tr[s, :, 3::3], tr[s, :, 4::3], tr[s, :, 5::3]
+        held = first > 0
+        busy += (done.max(axis=1) - x_) / 1e3
+        rows.setdefault(kinds[s % per_layer], []).append({
+            "barrier_us": np.median(b - e) / 1e3, "staging_us": np.median(x_ - b) / 1e3,
+            "first_wait_us": np.median((first - x_[:, None])[held]) / 1e3,
+            "run_us": np.median((run - first)[held]) / 1e3,
+            "cta_span_us": np.median(done.max(axis=1) - x_) / 1e3,
+            "enter_skew_us": (e.max() - e.min()) / 1e3})
+    out["stages"] = {k: {m: round(float(np.median([r[m] for r in v])), 2) for m in v[0]} for k, v in rows.items()}
+    out["cta_busy_per_layer_us_p0_50_100"] = [round(float(q), 2) for q in np.percentile(busy / (layers - 1), [0, 50, 100])]
+    return out
+
+
 # ---------------------------------------------------------------- reference arm
 
 def run_reference(args, rank, world):
@@ -570,6 +604,9 @@ def main(argv=None):
     parser.add_argument("--quick", action="store_true", help="fewer rounds and shapes (smoke runs)")
     parser.add_argument("--gather", choices=("nccl", "p2p"), default="p2p",
                         help="N>1: NCCL all-gathers, or gathers fused into the projections over NVLink")
+    parser.add_argument("--trace", action="store_true",
+                        help="persistent chain: after the timed steps, record one step's global-timer "
+                             "stamps (ProjectionChain.trace_step) and add a per-stage summary (not timed)")
     parser.add_argument("--stages-per-layer", type=int, choices=(2, 4), default=2,
                         help="persistent chain: stages per layer (ProjectionChain.persistent_schedule)")
     parser.add_argument("--persistent", action=argparse.BooleanOptionalAction, default=None,
@@ -656,6 +693,14 @@ def main(argv=None):
     t3 = time.perf_counter()
     e2e_s = all_max(torch, t3 - t2, world)
 
+    timeline = None
+    if args.trace and args.persistent:
+        tr = chain.trace_step(x)            # every rank runs the traced step
+        if rank == 0:
+            timeline = chain_timeline(tr.numpy(), len(chain.persistent_schedule()),
+                                      [kind for kind, _ in chain.persistent_schedule()])
+        barrier(world)
+
     launches = chain.launches_per_step()
     roofline = bench_dominant_kernel(torch, chain, peak)
     roofline["peak_kind"] = peak_kind
@@ -711,6 +756,8 @@ def main(argv=None):
             line["decode_attention"] = attention
         if prefetch is not None:
             line["l2_prefetch"] = prefetch
+        if timeline is not None:
+            line["timeline"] = timeline
         print(json.dumps(line), flush=True)
 
     if chain is not None:
