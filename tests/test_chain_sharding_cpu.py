@@ -122,3 +122,41 @@ def test_p2p_mode_argument_checks():
         ProjectionChain(shape, gather="mpi", project=lambda *a: None)
     with pytest.raises(ValueError):
         ProjectionChain(shape, world=2, gather="p2p", project=lambda *a: None)
+
+
+@pytest.mark.parametrize("stages_per_layer", [2, 4])
+def test_persistent_schedule_covers_every_row_once(stages_per_layer):
+    """Both persistent schedules list every row of q, k, v, o, gate, up and down exactly
+    once per layer; the two-stage schedule leads with the gathered up rows and keeps every
+    row that reads h_i in the first stage (host logic, oracle projection on CPU)."""
+    from klab_b200.chain import ChainShape, ProjectionChain
+
+    shape = ChainShape(**SHAPE)
+    for world, rank in ((1, 0), (2, 1)):
+        chain = ProjectionChain(shape, rank=rank, world=world,
+                                weights=lambda layer, name, rows: _weights(layer, name, rows, shape),
+                                project=_oracle_project, stages_per_layer=stages_per_layer)
+        sched = chain.persistent_schedule()
+        assert len(sched) == stages_per_layer
+        covered = {}
+        for _, parts in sched:
+            for name, b, e in parts:
+                n = chain.layers[0][name][1][1] - chain.layers[0][name][1][0]
+                e = n if e is None else e
+                covered.setdefault(name, []).append((b, e))
+        for name in ("q", "k", "v", "o", "gate", "up", "down"):
+            n = chain.layers[0][name][1][1] - chain.layers[0][name][1][0]
+            spans = sorted(covered[name])
+            assert spans[0][0] == 0 and spans[-1][1] == n, (name, spans)
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:])), (name, spans)
+        kinds = [kind for kind, _ in sched]
+        assert kinds.index("up") < kinds.index("down")
+        if stages_per_layer == 2:
+            assert sched[0][1][0][0] == "up" and [n for n, _, _ in sched[1][1]] == ["down"]
+
+
+def test_stages_per_layer_is_checked():
+    from klab_b200.chain import ChainShape, ProjectionChain
+
+    with pytest.raises(ValueError):
+        ProjectionChain(ChainShape(layers=1, hidden=64, kv=32, ffn=128), project=lambda *a: None, stages_per_layer=3)
