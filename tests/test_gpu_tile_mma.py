@@ -203,3 +203,19 @@ def test_cuda_core_route_still_meets_the_oracle(native, fmt):
         native.set_option(native.OPT_TENSOR, 3)
     report = ob.check_outputs(ref, y.float().cpu().numpy(), output_dtype="bf16")
     assert report["passed"] and report["max_ulp_error"] <= 1, report
+
+
+@pytest.mark.parametrize("fmt", FORMATS)
+def test_unaligned_x_uses_16_bit_staging(fmt):
+    """x starting 2 bytes past a 16-byte boundary (a contiguous view at storage offset 1):
+    the tiles stage it with 16-bit loads and meet the same oracle bound."""
+    m, n, k = 3, 90, 2048
+    lin, deq = make(fmt, n, k, 19)
+    x_bits = og.normal_bf16_bits(20, (m, k), 1.0)
+    flat = torch.empty(m * k + 8, dtype=torch.bfloat16, device="cuda")
+    x = flat[1:1 + m * k].view(m, k)
+    x.copy_(dev_bf16(x_bits))
+    assert x.data_ptr() % 16 == 2 and x.is_contiguous()
+    ref = og.projection64(ob.bf16_values(x_bits), deq)
+    report = ob.check_outputs(ref, lin(x, torch.bfloat16).float().cpu().numpy(), output_dtype="bf16")
+    assert report["passed"] and report["max_ulp_error"] <= 1, report
