@@ -57,13 +57,17 @@ def test_klab_run_and_check_end_to_end(tmp_path):
     from klab_b200.build import build_launcher
 
     klab = build_launcher()
+    # The launcher runs in the project root (like the reference's), so --output is relative to it;
+    # build/ is ignored by git.
+    result = ROOT / "build" / "klab_run_test.json"
     r = subprocess.run([str(klab), "run", "bf16-projection", "--shape", "1,2048,4096", "--rounds", "3", "--json",
-                        "--output", "results/klab_run_test.json"], cwd=tmp_path, capture_output=True, text=True,
+                        "--output", "build/klab_run_test.json"], cwd=tmp_path, capture_output=True, text=True,
                        timeout=600)
     assert r.returncode == 0, r.stderr
     row = json.loads(r.stdout)
     assert row["shape_mnk"] == [1, 2048, 4096] and row["us"] > 0 and row["cublas_us"] > 0
-    assert json.loads((tmp_path / "results" / "klab_run_test.json").read_text())["us"] == row["us"]
+    assert json.loads(result.read_text())["us"] == row["us"]
+    result.unlink()
     r = subprocess.run([str(klab), "check", "fp4-projection", "--json"], cwd=ROOT, capture_output=True, text=True,
                        timeout=900)
     assert r.returncode == 0, (r.stdout, r.stderr)
