@@ -117,6 +117,20 @@ def test_workspace_sizes():
     assert need >= 512 * 7 * 4 + 512 * 4
 
 
+@pytest.mark.parametrize("m", [1, 2, 4, 8, 9, 16])
+def test_workspace_covers_the_token_tiles(m):
+    """INT8 per-row and E2M1 weights at M <= 16 may run as warp-level tensor-core token tiles,
+    which keep FP32 phase partials [row group][phase][M][16] after the 64 KiB of tickets
+    (phases of 1024 INT8 / 2048 E2M1 columns): the advertised workspace holds them."""
+    from klab_b200 import _native
+
+    lib = _native.lib()
+    for wfmt, ks in ((_native.W_I8_ROW, 1024), (_native.W_FP4_G32H, 2048)):
+        for n, k in ((14336, 4096), (8192, 8192), (100, 2048), (4100, 2560)):
+            groups, phases = -(-n // 16), -(-k // ks)
+            assert lib.klab_gemv_workspace_bytes(wfmt, m, n, k) >= 65536 + groups * phases * m * 16 * 4, (wfmt, n, k)
+
+
 @pytest.mark.parametrize("shape", [(1024, 64), (3, 129), (48, 320), (5, 1), (2, 4096)])
 def test_host_codec_matches_oracle(shape):
     from klab_b200 import compressed_bf16 as cb
