@@ -41,13 +41,13 @@ PROBLEMS = [
                "tests/test_gpu_prepared.py", "tests/test_gpu_half_x.py"]},
     {"id": "int8-projection", "config": "c2", "default_shape": (1, 14336, 4096),
      "precision": "INT8 weights (per-row or per-64 FP32 scales), FP32 accumulation",
-     "description": "INT8 weight-only projection, CUDA-core and tcgen05 token tiles",
+     "description": "INT8 weight-only projection: CUDA-core, warp-level tensor-core and tcgen05 token tiles",
      "tests": ["tests/test_gpu_baseline_configs.py::test_c2_int8_per_row_14336x4096",
-               "tests/test_gpu_tensor_core.py"]},
+               "tests/test_gpu_tensor_core.py", "tests/test_gpu_tile_mma.py"]},
     {"id": "fp4-projection", "config": "c3", "default_shape": (1, 8192, 8192),
      "precision": "E2M1 weights (FP16/32 or E4M3/16 + global scales), FP32 accumulation",
-     "description": "FP4 weight projection with decode in registers",
-     "tests": ["tests/test_gpu_baseline_configs.py::test_c3_fp4_f16_scale_8192x8192"]},
+     "description": "FP4 weight projection with decode in registers; warp-level tensor-core token tiles at M >= 2",
+     "tests": ["tests/test_gpu_baseline_configs.py::test_c3_fp4_f16_scale_8192x8192", "tests/test_gpu_tile_mma.py"]},
     {"id": "lossless-bf16-projection", "config": "c4", "default_shape": (1, 4096, 4096),
      "precision": "Exact BF16 (lossless exponent coding), FP32 accumulation",
      "description": "Lossless-coded BF16 projection, bit-identical to the raw projection",
