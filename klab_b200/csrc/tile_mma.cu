@@ -4,9 +4,10 @@
 // The CUDA-core projection spends one FMA per weight and token plus the weight decode;
 // here a warp multiplies a 16-row group of weights with up to 16 tokens per mma.sync,
 // so the weight bytes are read and decoded once per tile and the math is a few tensor
-// instructions per 512 weights. On B200, mma.sync runs at most one m16n8k16 per 8
-// cycles per SM sub-partition (measured), well above what HBM delivers per SM at these
-// shapes, so the tile keeps up with the weight stream up to M = 16.
+// instructions per 512 weights. On B200, mma.sync issues at most one m16n8k16 per 8
+// cycles per SM sub-partition with a 20-cycle latency (measured): the MMA rate covers
+// the weight stream up to M = 16, but with two warps per scheduler this kernel is
+// bound by dependency latency and by x staging and the fold around the stream.
 //
 // Operands are FP16 with FP32 accumulation on mma.m16n8k16 for both formats:
 //   x of token t in a K phase is staged in FP16: BF16 x is scaled by 2^s, s from the
